@@ -1,0 +1,109 @@
+// C-ABI entry points for the contractions: matmul, fused MLP and attention.
+// Each picks the tcgen05 tensor-core kernel when the operands are 16-bit and
+// TMA-describable, and the SIMT kernel otherwise (fp32, odd strides).  The
+// choice depends only on dtype/shape/alignment, never on the data, so a given
+// call is bitwise reproducible.
+#include "ak_common.cuh"
+
+#include <cstdlib>
+
+namespace ak {
+bool tc_gemm_ok(int dtype, const void* A, const void* B, const void* B2, int64_t K, int64_t lda,
+                int64_t ldb, bool b_mn);
+int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, void* C, int M,
+            int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, cudaStream_t st);
+int simt_gemm_any(int dtype, const void* A, const void* B, const void* B2, void* C, int M, int N,
+                  int K, int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int act,
+                  cudaStream_t s);
+int simt_attention_any(int dtype, const void* Q, const void* K, const void* V, void* O,
+                       int64_t bh, int Sq, int Sk, int D, int causal, float scale,
+                       cudaStream_t s);
+bool tc_attention_ok(int dtype, const void* Q, const void* K, const void* V, const void* O,
+                     int D);
+int tc_attention(int dtype, const void* Q, const void* K, const void* V, void* O, int64_t bh,
+                 int Sq, int Sk, int D, int causal, float scale, cudaStream_t s);
+
+// Route every contraction through the SIMT kernels: set by ak_set_force_simt()
+// or, at load time, by the environment variable AK_FORCE_SIMT=1.
+static int g_force_simt = [] {
+  const char* e = getenv("AK_FORCE_SIMT");
+  return (e && e[0] == '1') ? 1 : 0;
+}();
+}  // namespace ak
+
+using namespace ak;
+
+extern "C" void ak_set_force_simt(int on) { g_force_simt = on; }
+
+extern "C" int ak_matmul(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                         int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int dtype,
+                         void* stream) {
+  AK_REQUIRE(dtype_ok(dtype), AK_ERR_DTYPE, "unsupported dtype %d", dtype);
+  AK_REQUIRE(M >= 0 && N >= 0 && K >= 0, AK_ERR_SHAPE, "negative shape");
+  AK_REQUIRE(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), AK_ERR_SHAPE,
+             "dimension exceeds 2^31-1");
+  AK_REQUIRE(lda >= K && ldc >= N && ldb >= (b_kmajor ? K : N), AK_ERR_SHAPE,
+             "leading dimension too small");
+  if (M == 0 || N == 0) return AK_OK;
+  AK_REQUIRE(A && B && C, AK_ERR_ARG, "null tensor pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (K == 0) {
+    // empty contraction: C = 0
+    cudaError_t e = cudaSuccess;
+    const size_t es = dtype_size(dtype);
+    e = cudaMemset2DAsync(C, ldc * es, 0, N * es, M, st);
+    AK_REQUIRE(e == cudaSuccess, AK_ERR_LAUNCH, "memset: %s", cudaGetErrorString(e));
+    return AK_OK;
+  }
+  if (!g_force_simt && tc_gemm_ok(dtype, A, B, nullptr, K, lda, ldb, !b_kmajor) &&
+      (b_kmajor || N % 8 == 0))
+    return tc_gemm(dtype, b_kmajor ? 0 : 1, A, B, nullptr, C, (int)M, (int)N, (int)K, lda, ldb,
+                   ldc, 0, st);
+  return simt_gemm_any(dtype, A, B, nullptr, C, (int)M, (int)N, (int)K, lda, ldb, ldc, b_kmajor,
+                       0, st);
+}
+
+extern "C" int ak_mlp_gate_up(const void* x, const void* w_gate, const void* w_up, void* hidden,
+                              int64_t M, int64_t D, int64_t H, int activation, int dtype,
+                              void* stream) {
+  AK_REQUIRE(dtype_ok(dtype), AK_ERR_DTYPE, "unsupported dtype %d", dtype);
+  AK_REQUIRE(activation >= AK_ACT_SILU && activation <= AK_ACT_RELU2, AK_ERR_ARG,
+             "unknown activation %d", activation);
+  AK_REQUIRE(M >= 0 && D >= 0 && H >= 0 && M < (1LL << 31) && D < (1LL << 31) &&
+                 H < (1LL << 31),
+             AK_ERR_SHAPE, "bad shape");
+  if (M == 0 || H == 0) return AK_OK;
+  AK_REQUIRE(x && w_gate && w_up && hidden, AK_ERR_ARG, "null tensor pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!g_force_simt && D > 0 && tc_gemm_ok(dtype, x, w_gate, w_up, D, D, D, false))
+    return tc_gemm(dtype, 2, x, w_gate, w_up, hidden, (int)M, (int)H, (int)D, D, D, H,
+                   activation, st);
+  return simt_gemm_any(dtype, x, w_gate, w_up, hidden, (int)M, (int)H, (int)D, D, D, H, 1,
+                       activation, st);
+}
+
+extern "C" int ak_fused_mlp(const void* x, const void* w_gate, const void* w_up,
+                            const void* w_down, void* hidden, void* out, int64_t M, int64_t D,
+                            int64_t H, int activation, int dtype, void* stream) {
+  int rc = ak_mlp_gate_up(x, w_gate, w_up, hidden, M, D, H, activation, dtype, stream);
+  if (rc) return rc;
+  // out[M, D] = hidden[M, H] @ w_down[D, H]^T
+  return ak_matmul(hidden, w_down, out, M, D, H, H, H, D, 1, dtype, stream);
+}
+
+extern "C" int ak_flash_attention(const void* Q, const void* K, const void* V, void* O,
+                                  int64_t batch_heads, int64_t Sq, int64_t Sk, int64_t D,
+                                  int causal, float sm_scale, int dtype, void* stream) {
+  AK_REQUIRE(dtype_ok(dtype), AK_ERR_DTYPE, "unsupported dtype %d", dtype);
+  AK_REQUIRE(batch_heads >= 0 && Sq >= 0 && Sk >= 0 && D > 0, AK_ERR_SHAPE, "bad shape");
+  AK_REQUIRE(Sq < (1LL << 31) && Sk < (1LL << 31), AK_ERR_SHAPE, "sequence too long");
+  if (batch_heads == 0 || Sq == 0) return AK_OK;
+  AK_REQUIRE(Sk > 0, AK_ERR_SHAPE, "attention over zero keys");
+  AK_REQUIRE(Q && K && V && O, AK_ERR_ARG, "null tensor pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!g_force_simt && tc_attention_ok(dtype, Q, K, V, O, (int)D))
+    return tc_attention(dtype, Q, K, V, O, batch_heads, (int)Sq, (int)Sk, (int)D, causal,
+                        sm_scale, st);
+  return simt_attention_any(dtype, Q, K, V, O, batch_heads, (int)Sq, (int)Sk, (int)D, causal,
+                            sm_scale, st);
+}

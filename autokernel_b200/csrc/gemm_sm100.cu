@@ -1,0 +1,367 @@
+// Tensor-core GEMM for sm_100a: C[M,N] = A[M,K] @ B, bf16/fp16 in, fp32
+// accumulate in TMEM, input dtype out.  Serves matmul (reference.py:10-12),
+// and both halves of the fused MLP (reference.py:45-55):
+//   MODE_MN   B is [K, N] row-major (torch.matmul(A, B)); UMMA B is MN-major
+//   MODE_K    B is [N, K] row-major (x @ W^T, the down projection)
+//   MODE_DUAL two K-major weights Wg, Wu [H, K]: the epilogue writes
+//             act(x @ Wg^T) * (x @ Wu^T), the SwiGLU hidden, in one pass.
+//
+// Structure: persistent CTAs (one per SM, 192 threads), warp-specialised:
+//   warp 0      TMA producer: 4-stage ring of {A 128x64, B 256x64} tiles,
+//               128-byte swizzle, completion on per-stage mbarriers
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//               (M=128, N=256, K=16 per instruction), commits free each
+//               stage and publish a finished accumulator
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, convert, store
+// The accumulator is double-buffered in TMEM (2 x 256 of the 512 columns)
+// so the epilogue of tile i overlaps the main loop of tile i+1.  Tiles are
+// visited in GROUP_M-row bands so that concurrently running CTAs share A and
+// B panels in L2.  No split-K and no atomics: results are deterministic.
+// Every mbarrier wait is bounded (see sm100.cuh).
+#include "sm100.cuh"
+#include "ak_act.cuh"
+
+#include <cudaTypedefs.h>
+#include <mutex>
+
+namespace ak {
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool make_tmap(CUtensorMap* map, int dtype, int rank, const void* base, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled unavailable from the driver");
+    return false;
+  }
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) gs[i] = strides_bytes[i];
+  CUresult r = fn(map, dtype == AK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  (cuuint32_t)rank, const_cast<void*>(base), gd, gs, bx, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+    return false;
+  }
+  return true;
+}
+
+namespace gemm {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192, GROUP_M = 8;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
+constexpr int TMEM_COLS = 512;
+
+enum { MODE_K = 0, MODE_MN = 1, MODE_DUAL = 2 };
+
+struct Params {
+  int M, N, K;  // N = output columns (hidden columns in MODE_DUAL)
+  void* C;
+  int64_t ldc;
+  int tiles_m, tiles_n, num_tiles;
+  int act;
+  int vec_store;  // C rows are 16-byte aligned
+  uint32_t idesc;
+};
+
+AK_D void tile_coords(int t, const Params& p, int& tm, int& tn) {
+  const int group = GROUP_M * p.tiles_n;
+  const int g = t / group;
+  const int first = g * GROUP_M;
+  const int gsz = min(p.tiles_m - first, GROUP_M);
+  const int r = t - g * group;
+  tm = first + r % gsz;
+  tn = r / gsz;
+}
+
+template <int DT>
+AK_D void store_row32(const Params& p, int row, int col, const float* v) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  if (row >= p.M) return;
+  T* c = reinterpret_cast<T*>(p.C) + (int64_t)row * p.ldc + col;
+  if (p.vec_store && col + 32 <= p.N) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 raw;
+      T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) e[j] = E::from_f(v[q * 8 + j]);
+      reinterpret_cast<uint4*>(c)[q] = raw;
+    }
+  } else {
+    for (int j = 0; j < 32 && col + j < p.N; ++j) c[j] = E::from_f(v[j]);
+  }
+}
+
+template <int DT, int MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                const __grid_constant__ CUtensorMap tb2, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  __shared__ uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&ta);
+    tma_prefetch_desc(&tb);
+    if (MODE == MODE_DUAL) tma_prefetch_desc(&tb2);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort_p = &abort_flag;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------- TMA producer
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, p, tm, tn);
+        const int m0 = tm * BM;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_p)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          const int k0 = kb * BK;
+          tma_load_2d(sa, &ta, &full[s], k0, m0);
+          if (MODE == MODE_K) {
+            tma_load_2d(sb, &tb, &full[s], k0, tn * BN);
+          } else if (MODE == MODE_DUAL) {
+            tma_load_2d(sb, &tb, &full[s], k0, tn * (BN / 2));
+            tma_load_2d(sb + B_BYTES / 2, &tb2, &full[s], k0, tn * (BN / 2));
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(sb + c * (64 * BK * 2), &tb, &full[s], tn * BN + c * 64, k0);
+          }
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---------------- MMA issuer
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      int it = 0;
+      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++it) {
+        const int b = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[b], aph ^ 1, abort_p)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_p)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = desc_kmajor(sa + k * 32);
+            const uint64_t bd = (MODE == MODE_MN) ? desc_mnmajor(sb + k * 16 * 128, 64 * BK * 2)
+                                                  : desc_kmajor(sb + k * 32);
+            umma_ss(d, ad, bd, p.idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (ok) umma_commit(&acc_full[b]);
+      }
+    }
+  } else {  // ---------------- epilogue warps 2..5
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int it = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
+      const int b = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      // one lane waits, the warp follows: tcgen05.ld below is warp-collective
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(&acc_full[b], aph, abort_p) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      const int row = tm * BM + q * 32 + lane;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * BN;
+      if (MODE != MODE_DUAL) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          store_row32<DT>(p, row, tn * BN + c, v);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tbase + c, g);
+          tmem_ld32(tbase + BN / 2 + c, u);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = apply_act(p.act, __uint_as_float(g[j])) * __uint_as_float(u[j]);
+          store_row32<DT>(p, row, tn * (BN / 2) + c, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+template <int DT, int MODE>
+static int launch(const void* A, const void* B, const void* B2, void* C, int M, int N, int K,
+                  int64_t lda, int64_t ldb, int64_t ldc, int act, cudaStream_t st) {
+  CUtensorMap ta, tb, tb2;
+  {
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, str[1] = {(uint64_t)lda * 2};
+    uint32_t box[2] = {BK, BM};
+    if (!make_tmap(&ta, DT, 2, A, dims, str, box)) return AK_ERR_LAUNCH;
+  }
+  if (MODE == MODE_MN) {
+    uint64_t dims[2] = {(uint64_t)N, (uint64_t)K}, str[1] = {(uint64_t)ldb * 2};
+    uint32_t box[2] = {64, BK};
+    if (!make_tmap(&tb, DT, 2, B, dims, str, box)) return AK_ERR_LAUNCH;
+    tb2 = tb;
+  } else {
+    const uint32_t rows = MODE == MODE_DUAL ? BN / 2 : BN;
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)N}, str[1] = {(uint64_t)ldb * 2};
+    uint32_t box[2] = {BK, rows};
+    if (!make_tmap(&tb, DT, 2, B, dims, str, box)) return AK_ERR_LAUNCH;
+    if (MODE == MODE_DUAL) {
+      if (!make_tmap(&tb2, DT, 2, B2, dims, str, box)) return AK_ERR_LAUNCH;
+    } else {
+      tb2 = tb;
+    }
+  }
+  Params p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = C;
+  p.ldc = ldc;
+  p.tiles_m = (M + BM - 1) / BM;
+  const int bn_out = MODE == MODE_DUAL ? BN / 2 : BN;
+  p.tiles_n = (N + bn_out - 1) / bn_out;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.act = act;
+  p.vec_store = (ldc % 8 == 0) && aligned16(C);
+  p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, BM, BN, false, MODE == MODE_MN);
+
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(gemm_kernel<DT, MODE>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  AK_REQUIRE(attr_err == cudaSuccess, AK_ERR_LAUNCH, "gemm: smem attribute: %s",
+             cudaGetErrorString(attr_err));
+  int grid = device_info().sm_count;
+  if (grid > p.num_tiles) grid = p.num_tiles;
+  gemm_kernel<DT, MODE><<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, tb2, p);
+  return launch_status("tc_gemm");
+}
+
+}  // namespace gemm
+
+// Tensor-core eligibility: 16-bit types, TMA-describable operands (16-byte
+// aligned bases, row strides that are 16-byte multiples).
+bool tc_gemm_ok(int dtype, const void* A, const void* B, const void* B2, int64_t K, int64_t lda,
+                int64_t ldb, bool b_mn) {
+  if (dtype != AK_F16 && dtype != AK_BF16) return false;
+  if (!aligned16(A) || !aligned16(B) || (B2 && !aligned16(B2))) return false;
+  if (lda % 8 || ldb % 8 || K % 8) return false;
+  (void)b_mn;
+  return device_info().cc_major == 10;
+}
+
+int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, void* C, int M,
+            int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, cudaStream_t st) {
+  using namespace gemm;
+#define AK_TCG(D)                                                                             \
+  if (mode == MODE_K) return launch<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, st); \
+  if (mode == MODE_MN) return launch<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, st); \
+  return launch<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, st);
+  if (dtype == AK_BF16) { AK_TCG(AK_BF16) }
+  AK_TCG(AK_F16)
+#undef AK_TCG
+}
+
+}  // namespace ak

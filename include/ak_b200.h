@@ -1,0 +1,169 @@
+/*
+ * ak_b200.h -- C ABI of libak_b200.so, the sm_100a (B200) implementation of
+ * AutoKernel's nine-operator kernel_fn contract.
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers, element counts and element strides; no framework
+ *     types.  `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Work is enqueued asynchronously on that stream.
+ *   - The caller allocates every input, output and workspace buffer; the
+ *     library never allocates device memory.
+ *   - Return AK_OK (0) or a negative AK_ERR_* code; ak_last_error() returns a
+ *     thread-local message for the last failure.  Nothing aborts or traps.
+ *   - dtype is one of AK_F32 / AK_F16 / AK_BF16; arithmetic accumulates in
+ *     fp32 (fp64 for cross-CTA sums), results are bitwise deterministic for a
+ *     given device, shape and dtype.
+ *
+ * Each declaration names the reference interface it replaces.  Paths are
+ * relative to the AutoKernel repository root.
+ */
+#ifndef AK_B200_H_
+#define AK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AK_API __attribute__((visibility("default")))
+#else
+#define AK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AK_VERSION 1
+
+enum ak_dtype { AK_F32 = 0, AK_F16 = 1, AK_BF16 = 2 };
+
+enum ak_status {
+  AK_OK = 0,
+  AK_ERR_ARG = -1,         /* null pointer, bad workspace, bad enum */
+  AK_ERR_DTYPE = -2,       /* dtype not supported by this op */
+  AK_ERR_SHAPE = -3,       /* inconsistent or out-of-range sizes */
+  AK_ERR_ALIGN = -4,       /* alignment the op cannot handle */
+  AK_ERR_LAUNCH = -5,      /* CUDA launch / driver error */
+  AK_ERR_UNSUPPORTED = -6  /* feature not available on this device */
+};
+
+enum ak_activation { AK_ACT_SILU = 0, AK_ACT_GELU = 1, AK_ACT_RELU2 = 2 };
+
+/* Codes written to the device status word by bounded spin-waits. */
+#define AK_STATUS_TIMEOUT 1
+
+/* ----------------------------------------------------------------- utilities */
+AK_API const char* ak_last_error(void);
+AK_API int ak_version(void);
+/* Reads (and optionally clears) the device status word; synchronous. */
+AK_API int ak_device_status(int clear);
+AK_API int ak_sm_count(void);
+/* Test hook: 1 routes matmul/MLP/attention through the SIMT kernels. */
+AK_API void ak_set_force_simt(int on);
+
+/* ----------------------------------------------------------------- row ops */
+
+/* y = x / sqrt(mean(x^2, -1) + eps) * w over rows of length `cols`.
+ * Replaces kernels/rmsnorm.py:45 kernel_fn(x, weight, eps) and
+ * kernels/cuda/rmsnorm.py:171 (reference oracle reference.py:26-29). */
+AK_API int ak_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t cols, int64_t ldx,
+               int64_t ldy, float eps, int dtype, void* stream);
+
+/* y = (x - mean) / sqrt(var + eps) * w + b over rows.
+ * Replaces kernels/layernorm.py:65 kernel_fn(x, weight, bias, eps)
+ * (reference.py:20-23). */
+AK_API int ak_layernorm(const void* x, const void* w, const void* b, void* y, int64_t rows,
+                 int64_t cols, int64_t ldx, int64_t ldy, float eps, int dtype, void* stream);
+
+/* y = softmax(x, -1) over rows.  Replaces kernels/softmax.py:57 kernel_fn(x)
+ * (reference.py:15-17). */
+AK_API int ak_softmax(const void* x, void* y, int64_t rows, int64_t cols, int64_t ldx, int64_t ldy,
+               int dtype, void* stream);
+
+/* Interleaved-pair RoPE on contiguous x/y [rows, head_dim]; cos/sin are
+ * contiguous [cs_rows, head_dim/2] and row r uses cos/sin row
+ * (r / cs_div) % cs_rows.  cs_dtype is dtype or AK_F32.
+ * Replaces kernels/rotary_embedding.py:75 kernel_fn(x, cos, sin)
+ * (reference.py:63-69). */
+AK_API int ak_rotary_embedding(const void* x, const void* cos, const void* sin, void* y, int64_t rows,
+                        int64_t head_dim, int64_t cs_div, int64_t cs_rows, int dtype,
+                        int cs_dtype, void* stream);
+
+/* ----------------------------------------------------------------- reductions */
+
+/* out[o, i] = sum_r x[o, r, i] for contiguous x viewed as [outer, n, inner].
+ * Replaces kernels/reduce.py:51 kernel_fn(x, dim) (reference.py:72-74). */
+AK_API int ak_reduce_sum(const void* x, void* out, int64_t outer, int64_t n, int64_t inner, int dtype,
+                  int out_dtype, void* stream);
+
+/* Bytes of workspace ak_reduce_sum_full needs on the current device. */
+AK_API size_t ak_reduce_workspace_size(void);
+
+/* Sum of all n elements of contiguous x.  Writes the fp64 total to *total
+ * (device pointer, may be NULL) and, if out != NULL, the total cast to
+ * out_dtype to *out.  The fp64 total is the per-rank partial that a sharded
+ * caller all-reduces.  Same reference entry as ak_reduce_sum, for 1-D x. */
+AK_API int ak_reduce_sum_full(const void* x, int64_t n, int dtype, double* total, void* out,
+                       int out_dtype, void* workspace, size_t ws_bytes, void* stream);
+
+/* *out = (out_dtype) *total (both device pointers). */
+AK_API int ak_scalar_from_sum(const double* total, void* out, int out_dtype, void* stream);
+
+/* Per-row cross entropy: row_loss[r] = logsumexp(logits[r]) - logits[r, t_r]
+ * (0 where t_r == ignore_index).  row_max / row_target_logit (optional, may
+ * be NULL) receive the row max and the gathered target logit as fp32; both
+ * are exact copies of input values.  *bad_target (optional) is set to 1 if a
+ * target is outside [0, vocab) and not ignore_index.
+ * Replaces kernels/cross_entropy.py:70 kernel_fn(logits, targets)
+ * (reference.py:58-60). */
+AK_API int ak_cross_entropy_rows(const void* logits, const int64_t* targets, int64_t rows,
+                          int64_t vocab, int64_t ld, int dtype, int64_t ignore_index,
+                          float* row_loss, float* row_max, float* row_target_logit,
+                          int* bad_target, void* stream);
+
+/* Fixed-order fp64 sum of row_loss over non-ignored rows.  sum_count (device,
+ * may be NULL) receives {sum, count}; out (may be NULL) receives sum/count in
+ * out_dtype. */
+AK_API int ak_cross_entropy_finalize(const float* row_loss, const int64_t* targets, int64_t rows,
+                              int64_t ignore_index, double* sum_count, void* out,
+                              int out_dtype, void* stream);
+
+/* *out = sum_count[0] / sum_count[1] in out_dtype (after an all-reduce). */
+AK_API int ak_mean_from_sum_count(const double* sum_count, void* out, int out_dtype, void* stream);
+
+/* ----------------------------------------------------------------- contractions */
+
+/* C[M, N] = A[M, K] @ B where B is [K, N] row-major (b_kmajor = 0) or the
+ * transpose of an [N, K] row-major matrix (b_kmajor = 1).  Leading
+ * dimensions in elements.  Replaces kernels/matmul.py:62 kernel_fn(A, B) and
+ * kernels/cuda/matmul.py:246 (reference.py:10-12). */
+AK_API int ak_matmul(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+              int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int dtype, void* stream);
+
+/* hidden[M, H] = act(x @ w_gate^T) * (x @ w_up^T) for contiguous x [M, D],
+ * w_gate / w_up [H, D].  First stage of kernels/fused_mlp.py:102. */
+AK_API int ak_mlp_gate_up(const void* x, const void* w_gate, const void* w_up, void* hidden, int64_t M,
+                   int64_t D, int64_t H, int activation, int dtype, void* stream);
+
+/* out[M, D] = (act(x @ w_gate^T) * (x @ w_up^T)) @ w_down^T with w_down
+ * [D, H]; `hidden` is caller workspace of M*H elements of dtype.
+ * Replaces kernels/fused_mlp.py:102 kernel_fn(x, w_gate, w_up, w_down,
+ * activation) (reference.py:45-55). */
+AK_API int ak_fused_mlp(const void* x, const void* w_gate, const void* w_up, const void* w_down,
+                 void* hidden, void* out, int64_t M, int64_t D, int64_t H, int activation,
+                 int dtype, void* stream);
+
+/* O = softmax(Q K^T * sm_scale [+ causal mask]) V for contiguous Q/O
+ * [batch_heads, Sq, D] and K/V [batch_heads, Sk, D].  The causal mask hides
+ * key j from query i when j > i (top-left aligned, like
+ * torch.triu(ones(Sq, Sk), 1)).  Replaces kernels/flash_attention.py:130
+ * kernel_fn(Q, K, V, causal, sm_scale) (reference.py:32-42). */
+AK_API int ak_flash_attention(const void* Q, const void* K, const void* V, void* O,
+                       int64_t batch_heads, int64_t Sq, int64_t Sk, int64_t D, int causal,
+                       float sm_scale, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AK_B200_H_ */
