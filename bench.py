@@ -253,7 +253,7 @@ def ours(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=device)
     pk = peaks()
-    d = W.sweep_inputs(device, seed=rank)
+    d = W.sweep_inputs(device, seed=rank, scale=args.scale)
     bytes_per = W.sweep_bytes(d)
     step_bytes = sum(bytes_per.values())
     torch.cuda.synchronize()
@@ -349,13 +349,13 @@ def _cpu_sample():
     g = torch.Generator().manual_seed(0)
     bf = torch.bfloat16
     d = {
-        "sm_x": (torch.randn(128, 32768, generator=g) * 2).to(bf),
-        "ln_x": torch.randn(512, 4096, generator=g).to(bf),
+        "sm_x": (torch.randn(1024, 32768, generator=g) * 2).to(bf),
+        "ln_x": torch.randn(4096, 4096, generator=g).to(bf),
         "ln_w": (1 + 0.1 * torch.randn(4096, generator=g)).to(bf),
         "ln_b": (0.1 * torch.randn(4096, generator=g)).to(bf),
-        "q": torch.randn(1, 4, 4096, 128, generator=g).to(bf),
-        "k": torch.randn(1, 4, 4096, 128, generator=g).to(bf),
-        "red_x": torch.rand(1 << 25, generator=g) * 2 - 1,
+        "q": torch.randn(1, 32, 4096, 128, generator=g).to(bf),
+        "k": torch.randn(1, 32, 4096, 128, generator=g).to(bf),
+        "red_x": torch.rand(1 << 27, generator=g) * 2 - 1,
     }
     inv = 1.0 / 10000.0 ** (torch.arange(0, 128, 2).float() / 128)
     ang = torch.outer(torch.arange(4096).float(), inv)
@@ -387,8 +387,9 @@ def cpu_baseline(seconds: float) -> dict:
         n += 1
     dt = (time.perf_counter() - t0) / n
     return {"value": round(nbytes / dt / 1e9, 2), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"reference.py ops restated on CPU tensors (oracle/ref_torch.py): softmax 128 rows, "
-                      f"layernorm 512 rows, rope 1x4 heads (q,k), reduce 2^25; same shapes per row; "
+            "sample": f"reference.py ops restated on CPU tensors (oracle/ref_torch.py): softmax 1024 rows, "
+                      f"layernorm 4096 rows, rope 1x32 heads (q,k), reduce 2^27; same shapes per row, "
+                      f"sample larger than the last-level cache; "
                       f"{n} reps in {seconds:.0f}s; {nbytes / 1e9:.3f} GB per rep",
             "cpu_model": _cpu_model()}
 
@@ -424,8 +425,8 @@ def reference_arm(args):
         "vs_baseline": None, "dtype": "bf16 (reduce: fp32)", "data": "synthetic (seeded)",
         "config": {"workload": "configs[1] memory-bound sweep, bounded CPU sample (rank 0 only)"},
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": "softmax 128x32768, layernorm 512x4096, rope q,k 1x4x4096x128, "
-                                   "reduce 2^25 fp32 per step (reference.py ops on CPU tensors)"},
+                         "sample": "softmax 1024x32768, layernorm 4096x4096, rope q,k 1x32x4096x128, "
+                                   "reduce 2^27 fp32 per step (reference.py ops on CPU tensors)"},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -444,6 +445,9 @@ def main(argv=None):
     ap.add_argument("--no-ops", action="store_true", help="skip the GEMM/MLP/attention/CE/RMSNorm lines")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--scale", type=float, default=1.0,
+                    help="shrink the sweep's leading dims (profiling captures only; the bench "
+                         "line is only valid at 1.0)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
