@@ -35,6 +35,7 @@ SIGNATURES = {
     "ak_reduce_sum": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ak_reduce_workspace_size": (_sz, []),
     "ak_reduce_sum_full": (_i32, [_vp, _i64, _i32, _vp, _vp, _i32, _vp, _sz, _vp]),
+    "ak_reduce_sum_full_noalloc": (_i32, [_vp, _i64, _i32, _vp, _vp, _i32, _vp]),
     "ak_scalar_from_sum": (_i32, [_vp, _vp, _i32, _vp]),
     "ak_cross_entropy_rows": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _i64, _vp, _vp, _vp, _vp, _vp]),
     "ak_cross_entropy_finalize": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _i32, _vp]),

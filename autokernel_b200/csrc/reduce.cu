@@ -20,6 +20,8 @@
 // fp64 and divides by the number of rows whose target is not ignore_index.
 #include "ak_common.cuh"
 
+#include <mutex>
+
 namespace ak {
 
 // ------------------------------------------------------------------ full sum
@@ -342,4 +344,75 @@ extern "C" int ak_mean_from_sum_count(const double* sum_count, void* out, int ou
   cudaStream_t st = (cudaStream_t)stream;
   AK_DISPATCH_DT(out_dtype, mean_from_sum_count_kernel, <<<1, 1, 0, st>>>(sum_count, out))
   return launch_status("mean_from_sum_count");
+}
+
+// ------------------------------------------------------------------ no-allocation variant
+// Some callers cannot call cudaMalloc at all: code that runs inside another framework's
+// memory pool or allocator callback, plugin hosts that forbid device allocation after
+// start-up, or real-time paths where an allocation (and its implicit synchronisation) is not
+// allowed.  They still need the full sum, whose first kernel writes one fp64 partial per CTA
+// into scratch memory.  ak_reduce_sum_full_noalloc keeps that scratch in this file-scope
+// device array instead of asking the caller for a workspace.
+//
+// The array is module memory: every GPU that loads the library holds it (16 KiB) until the
+// process exits.  Its host-side name is only a stand-in, so its device address is looked up
+// once per device with cudaGetSymbolAddress (with that device current) on the first call on
+// that device; make that first call before any stream capture.  All calls on a device share
+// the array and it keeps the last call's partials; every partial slot the final kernel reads
+// is rewritten by the partial kernel of the same call, so nothing needs clearing.  Calls that
+// overlap on the GPU (different streams, no ordering between them) race on the array.
+namespace ak {
+constexpr int kNoAllocMaxPartials = 2048;  // scratch capacity: fp64 partials (16 KiB)
+static __device__ __align__(256) double g_noalloc_partials[kNoAllocMaxPartials];
+
+static double* noalloc_scratch(int* err) {
+  static std::mutex mu;
+  static double* ptr[64] = {};
+  static bool done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = 1;
+    set_error("ak_reduce_sum_full_noalloc: no usable current device (%s)",
+              cudaGetErrorString(e));
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess || p == nullptr) {
+      *err = 1;
+      set_error("ak_reduce_sum_full_noalloc: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(e));
+      return nullptr;
+    }
+    ptr[dev] = static_cast<double*>(p);
+    done[dev] = true;
+  }
+  return ptr[dev];
+}
+}  // namespace ak
+
+extern "C" int ak_reduce_sum_full_noalloc(const void* x, int64_t n, int dtype, double* total,
+                                          void* out, int out_dtype, void* stream) {
+  AK_REQUIRE(dtype_ok(dtype) && dtype_ok(out_dtype), AK_ERR_DTYPE, "unsupported dtype");
+  AK_REQUIRE(n >= 0, AK_ERR_SHAPE, "negative n");
+  AK_REQUIRE(n == 0 || x, AK_ERR_ARG, "null input");
+  const int nb = partial_blocks();
+  AK_REQUIRE(nb <= kNoAllocMaxPartials, AK_ERR_SHAPE,
+             "ak_reduce_sum_full_noalloc: this device needs %d partial slots but the built-in "
+             "scratch holds at most %d; use ak_reduce_sum_full with a workspace",
+             nb, kNoAllocMaxPartials);
+  int err = 0;
+  double* partials = noalloc_scratch(&err);
+  if (err) return AK_ERR_LAUNCH;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (aligned16(x)) {
+    AK_DISPATCH_DT(dtype, reduce_partial_kernel, <<<nb, 512, 0, st>>>(x, n, partials))
+  } else {
+    AK_DISPATCH_DT(dtype, reduce_partial_scalar_kernel, <<<nb, 512, 0, st>>>(x, n, partials))
+  }
+  AK_DISPATCH_DT(out_dtype, reduce_final_kernel, <<<1, 1024, 0, st>>>(partials, nb, total, out))
+  return launch_status("reduce_sum_full_noalloc");
 }

@@ -106,6 +106,16 @@ AK_API size_t ak_reduce_workspace_size(void);
 AK_API int ak_reduce_sum_full(const void* x, int64_t n, int dtype, double* total, void* out,
                        int out_dtype, void* workspace, size_t ws_bytes, void* stream);
 
+/* Same result as ak_reduce_sum_full, for callers that cannot allocate device memory (they
+ * run inside another framework's allocator or a host that forbids cudaMalloc after start-up).
+ * No counterpart in the reference.  The per-CTA scratch lives in a 16 KiB array inside the
+ * library (held by every GPU that loads it until exit); the first call on a device looks up
+ * its address and should come before any stream capture.  Calls on one device share that
+ * array: calls that overlap on the GPU race.  Fails with AK_ERR_SHAPE if the device needs more
+ * than 2048 partial slots (4 per SM).  Allocates nothing. */
+AK_API int ak_reduce_sum_full_noalloc(const void* x, int64_t n, int dtype, double* total,
+                                      void* out, int out_dtype, void* stream);
+
 /* *out = (out_dtype) *total (both device pointers). */
 AK_API int ak_scalar_from_sum(const double* total, void* out, int out_dtype, void* stream);
 
