@@ -1,12 +1,363 @@
-// Tensor-core causal flash attention for sm_100a (placeholder: the tcgen05
-// kernel is not built yet, so every call takes the SIMT kernel).
-#include "ak_common.cuh"
+// Tensor-core flash attention for sm_100a (reference.py:32-42):
+//   O = softmax(Q K^T * scale [+ causal mask]) V,  Q/O [BH, Sq, D], K/V [BH, Sk, D],
+// bf16/fp16 in, fp32 softmax statistics and accumulators, D in {64, 128}.
+//
+// One CTA owns two 128-row query tiles (A, B) of one (batch, head) and walks the
+// key/value sequence in 128-key blocks.  320 threads, warp-specialised:
+//   warp 0      TMA producer: Q tiles once, then a 2-stage ring of {K, V} blocks
+//               (3-D tensor maps [BH, S, D], so tails zero-fill inside a head)
+//   warp 1      TMEM allocator (512 columns) + single-thread MMA issuer
+//   warps 2..5  softmax / epilogue of tile A, one thread per query row
+//   warps 6..9  softmax / epilogue of tile B
+// TMEM per tile: S = Q K^T (128 fp32 columns) and O (D columns).  The softmax
+// threads read their row of S, write P = exp2(S*scale*log2e - m) as packed 16-bit
+// pairs over the first 64 columns of S, and the MMA computes O += P V with P read
+// from TMEM (tcgen05.mma A-from-TMEM form) and V from shared memory (MN-major).
+// While tile A is in its softmax the tensor core works on tile B and vice versa.
+//
+// Online softmax with a lazily updated reference max: P is computed against the
+// row's current reference m; only when a new block raises the row max by more
+// than 8 (log2 units, so P stays <= 256) are O and l rescaled by exp2(m_old - m_new)
+// in TMEM.  The final O / l is exact up to rounding whatever m is.  Causal
+// blocks above the diagonal are skipped; the diagonal block and key tails are
+// masked to -inf before the exponent.
+//
+// Every mbarrier wait is bounded (sm100.cuh): on timeout the CTA unwinds, frees
+// its TMEM and records AK_STATUS_TIMEOUT in the device status word.
+#include "sm100.cuh"
+
+#include <mutex>
 
 namespace ak {
-bool tc_attention_ok(int, const void*, const void*, const void*, const void*, int) { return false; }
-int tc_attention(int, const void*, const void*, const void*, void*, int64_t, int, int, int, int,
-                 float, cudaStream_t) {
-  set_error("tensor-core attention not built");
-  return AK_ERR_UNSUPPORTED;
+namespace attn {
+
+using namespace sm100;
+
+constexpr int BQ = 128, BKV = 128, THREADS = 320;
+constexpr int CHUNK_BYTES = 128 * 64 * 2;  // one TMA box: 128 rows x 64 16-bit elements
+
+template <int D>
+struct Cfg {
+  static constexpr int NC = D / 64;                         // 64-wide chunks per row
+  static constexpr int TILE_BYTES = NC * CHUNK_BYTES;       // 128 rows x D
+  static constexpr int Q_OFF = 0;                           // 2 query tiles
+  static constexpr int K_OFF = 2 * TILE_BYTES;              // 2 stages of K
+  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;      // 2 stages of V
+  static constexpr int SMEM = V_OFF + 2 * TILE_BYTES + 1024;
+  static constexpr int TMEM_TILE = 256;                     // S (128) + O (<= 128)
+};
+
+struct Params {
+  void* O;
+  int Sq, Sk, BH;
+  int causal;
+  float scale_log2;  // sm_scale * log2(e)
+  uint32_t idesc_qk, idesc_pv;
+  int n_qblk;        // query blocks of 256 rows
+};
+
+template <int DT, int D>
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                const __grid_constant__ CUtensorMap tv, Params p) {
+  using C = Cfg<D>;
+  using E = Elem<DT>;
+  using T = typename E::T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  __shared__ uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_done[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int qblk = p.n_qblk - 1 - (int)blockIdx.y;  // heaviest (causal) blocks first
+  const int q0 = qblk * 2 * BQ;
+  // key blocks this CTA needs: all of them, or up to the diagonal of its last row
+  int n_kv = (p.Sk + BKV - 1) / BKV;
+  if (p.causal) {
+    const int last_row = min(q0 + 2 * BQ, p.Sq) - 1;
+    n_kv = min(n_kv, last_row / BKV + 1);
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort_p = &abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ------------------------------------------ TMA producer
+      mbar_expect_tx(&q_full, 2 * C::TILE_BYTES);
+      for (int x = 0; x < 2; ++x)
+        for (int c = 0; c < C::NC; ++c)
+          tma_load_3d(smem + C::Q_OFF + x * C::TILE_BYTES + c * CHUNK_BYTES, &tq, &q_full, c * 64,
+                      q0 + x * BQ, bh);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, abort_p)) break;
+        mbar_expect_tx(&k_full[st], C::TILE_BYTES);
+        for (int c = 0; c < C::NC; ++c)
+          tma_load_3d(smem + C::K_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tk, &k_full[st],
+                      c * 64, j * BKV, bh);
+        mbar_expect_tx(&v_full[st], C::TILE_BYTES);
+        for (int c = 0; c < C::NC; ++c)
+          tma_load_3d(smem + C::V_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tv, &v_full[st],
+                      c * 64, j * BKV, bh);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ------------------------------------------ MMA issuer
+      const uint32_t sq = smem_u32(smem + C::Q_OFF);
+      const uint32_t sk = smem_u32(smem + C::K_OFF);
+      const uint32_t sv = smem_u32(smem + C::V_OFF);
+      auto qk = [&](int x, int st) {  // S_x = Q_x K_st^T
+        const uint32_t d = tmem + x * C::TMEM_TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
+          umma_ss(d, desc_kmajor(sq + x * C::TILE_BYTES + off),
+                  desc_kmajor(sk + st * C::TILE_BYTES + off), p.idesc_qk, kk > 0);
+        }
+      };
+      auto pv = [&](int x, int st, bool acc) {  // O_x += P_x V_st
+        const uint32_t d = tmem + x * C::TMEM_TILE + 128;
+        const uint32_t a = tmem + x * C::TMEM_TILE;
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          umma_ts(d, a + kk * 8, desc_mnmajor(sv + st * C::TILE_BYTES + kk * 16 * 128, CHUNK_BYTES),
+                  p.idesc_pv, (acc || kk > 0) ? 1 : 0);
+      };
+      bool ok = mbar_wait(&q_full, 0, abort_p) && mbar_wait(&k_full[0], 0, abort_p);
+      if (ok) {
+        tc_fence_after();
+        qk(0, 0);
+        umma_commit(&s_full[0]);
+        qk(1, 0);
+        umma_commit(&s_full[1]);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j & 1;
+        for (int x = 0; x < 2 && ok; ++x) {
+          if (!mbar_wait(&p_full[x], j & 1, abort_p)) { ok = false; break; }
+          if (x == 0 && !mbar_wait(&v_full[st], (j >> 1) & 1, abort_p)) { ok = false; break; }
+          tc_fence_after();
+          pv(x, st, j > 0);
+          if (x == 1) umma_commit(&kv_empty[st]);
+          if (j == n_kv - 1) {
+            umma_commit(&o_done[x]);
+          } else {
+            const int nst = (j + 1) & 1;
+            if (x == 0 && !mbar_wait(&k_full[nst], ((j + 1) >> 1) & 1, abort_p)) { ok = false; break; }
+            tc_fence_after();
+            qk(x, nst);
+            umma_commit(&s_full[x]);
+          }
+        }
+      }
+    }
+  } else {  // ------------------------------------------------ softmax / epilogue
+    const int x = (warp - 2) >> 2;       // query tile 0 (warps 2..5) or 1 (warps 6..9)
+    const int quarter = warp & 3;        // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    const int qrow = q0 + x * BQ + row_in_tile;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t t_s = tmem + x * C::TMEM_TILE + lane_base;
+    const uint32_t t_o = t_s + 128;
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      int w = 0;
+      if (lane == 0) w = mbar_wait(&s_full[x], j & 1, abort_p) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+      tc_fence_after();
+      const int k0 = j * BKV;
+      // keys < kmax are visible to this row
+      int kmax = p.Sk - k0;
+      if (p.causal) kmax = min(kmax, qrow - k0 + 1);
+      // pass 1: row max of this block
+      float bmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_s + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c * 32 + i < kmax) bmax = fmaxf(bmax, __uint_as_float(r[i]));
+      }
+      bmax *= p.scale_log2;
+      // lazy rescale: move the reference max only when it grows by more than 8
+      if (bmax > m_ref + 8.f) {
+        const float m_new = bmax;
+        if (j > 0 && m_ref != -INFINITY) {
+          const float alpha = ex2_approx(m_ref - m_new);
+          l *= alpha;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(t_o + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(t_o + c * 32, r);
+          }
+          tmem_wait_st();
+        } else if (j > 0) {
+          // O holds only zeros from fully masked blocks; nothing to rescale
+        }
+        m_ref = m_new;
+      }
+      // pass 2: P = exp2(s * scale_log2 - m_ref), packed in pairs over S columns [0, 64)
+      float bsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32], pk[16];
+        tmem_ld32(t_s + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int k = c * 32 + 2 * i;
+          float a = (k < kmax && m_ref != -INFINITY)
+                        ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), p.scale_log2, -m_ref)) : 0.f;
+          float b = (k + 1 < kmax && m_ref != -INFINITY)
+                        ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), p.scale_log2, -m_ref)) : 0.f;
+          bsum += a + b;
+          if constexpr (DT == AK_BF16) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+            pk[i] = *reinterpret_cast<uint32_t*>(&h);
+          } else {
+            __half2 h = __floats2half2_rn(a, b);
+            pk[i] = *reinterpret_cast<uint32_t*>(&h);
+          }
+        }
+        tmem_st16(t_s + c * 16, pk);
+      }
+      l += bsum;
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[x]);
+    }
+    // epilogue: O / l -> global
+    int w = 0;
+    if (ok && lane == 0) w = mbar_wait(&o_done[x], 0, abort_p) ? 1 : 0;
+    w = __shfl_sync(0xffffffffu, w, 0);
+    if (w) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = reinterpret_cast<T*>(p.O) + ((int64_t)bh * p.Sq + qrow) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_o + c * 32, r);
+        tmem_wait_ld();
+        if (qrow < p.Sq) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 raw;
+            T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) e[i] = E::from_f(__uint_as_float(r[q * 8 + i]) * inv);
+            reinterpret_cast<uint4*>(orow + c * 32)[q] = raw;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
 }
+
+}  // namespace attn
+
+namespace attn {
+
+static bool make_tmap_3d(CUtensorMap* m, int dtype, const void* base, int S, int D, int64_t BH) {
+  uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)BH};
+  uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
+  uint32_t box[3] = {64, 128, 1};
+  return make_tmap(m, dtype, 3, base, dims, strides, box);
+}
+
+template <int DT, int D>
+static int launch(const void* Q, const void* K, const void* V, void* O, int64_t bh, int Sq,
+                  int Sk, int causal, float scale, cudaStream_t st) {
+  CUtensorMap tq, tk, tv;
+  if (!make_tmap_3d(&tq, DT, Q, Sq, D, bh) || !make_tmap_3d(&tk, DT, K, Sk, D, bh) ||
+      !make_tmap_3d(&tv, DT, V, Sk, D, bh))
+    return AK_ERR_LAUNCH;
+  Params p;
+  p.O = O;
+  p.Sq = Sq;
+  p.Sk = Sk;
+  p.BH = (int)bh;
+  p.causal = causal;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const int fmt = DT == AK_BF16 ? 1 : 0;
+  p.idesc_qk = idesc_f16(fmt, BQ, BKV, false, false);
+  p.idesc_pv = idesc_f16(fmt, BQ, D, false, true);
+  p.n_qblk = (Sq + 2 * BQ - 1) / (2 * BQ);
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(attn_kernel<DT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                Cfg<D>::SMEM);
+  });
+  AK_REQUIRE(attr == cudaSuccess, AK_ERR_LAUNCH, "attention smem attribute: %s",
+             cudaGetErrorString(attr));
+  dim3 grid((unsigned)bh, (unsigned)p.n_qblk);
+  attn_kernel<DT, D><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tq, tk, tv, p);
+  return launch_status("tc_attention");
+}
+
+}  // namespace attn
+
+bool tc_attention_ok(int dtype, const void* Q, const void* K, const void* V, const void* O,
+                     int D) {
+  if (dtype != AK_F16 && dtype != AK_BF16) return false;
+  if (D != 64 && D != 128) return false;
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return false;
+  return device_info().cc_major == 10;
+}
+
+int tc_attention(int dtype, const void* Q, const void* K, const void* V, void* O, int64_t bh,
+                 int Sq, int Sk, int D, int causal, float scale, cudaStream_t s) {
+  AK_REQUIRE(bh <= 0x7fffffffLL, AK_ERR_SHAPE, "batch*heads too large");
+  AK_REQUIRE((Sq + 255) / 256 <= 65535, AK_ERR_SHAPE, "sequence too long for the grid");
+  if (dtype == AK_BF16) {
+    if (D == 128) return attn::launch<AK_BF16, 128>(Q, K, V, O, bh, Sq, Sk, causal, scale, s);
+    return attn::launch<AK_BF16, 64>(Q, K, V, O, bh, Sq, Sk, causal, scale, s);
+  }
+  if (D == 128) return attn::launch<AK_F16, 128>(Q, K, V, O, bh, Sq, Sk, causal, scale, s);
+  return attn::launch<AK_F16, 64>(Q, K, V, O, bh, Sq, Sk, causal, scale, s);
+}
+
 }  // namespace ak
