@@ -148,6 +148,23 @@ AK_D void lse_merge(float& m, float& s, float m2, float s2) {
 
 AK_HD bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Division of 32-bit unsigned n by a run-time constant d with a multiply-high
+// (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", 1994): q = (umulhi(n, m) + n) >> l with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1.  Exact for n < 2^31 (the sum never
+// overflows 32 bits).  Built on the host, used in index arithmetic.
+struct FastDiv {
+  uint32_t d, m, l;
+  FastDiv() : d(1), m(0), l(0) {}
+  explicit FastDiv(uint32_t div) : d(div) {
+    l = 0;
+    while ((1ull << l) < div) ++l;
+    m = (uint32_t)(((1ull << 32) * ((1ull << l) - div)) / div + 1);
+  }
+  AK_D uint32_t div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
+  AK_D uint32_t mod(uint32_t n) const { return n - div(n) * d; }
+};
+
 struct DeviceInfo {
   int sm_count;
   int max_smem_optin;

@@ -19,6 +19,9 @@
 // per-row loss; the finalize kernel adds the per-row losses in fixed order in
 // fp64 and divides by the number of rows whose target is not ignore_index.
 #include "ak_common.cuh"
+#include "rowring.cuh"
+#include "packed.cuh"
+#include "sm100.cuh"
 
 #include <mutex>
 
@@ -206,6 +209,76 @@ __global__ void __launch_bounds__(512) xent_row_kernel(const void* logits, const
   }
 }
 
+// Streaming cross entropy for rows whose start and length are 16-byte
+// multiples: 256 threads per row, four 16-byte loads in flight per thread, a
+// packed max over each group of four vectors, then one running-max update and
+// exp2((x - m) log2e) per element.  One HBM read per logit.
+template <int DT>
+__global__ void __launch_bounds__(256) xent_stream_kernel(const void* logits,
+                                                          const int64_t* targets, int64_t vocab,
+                                                          int64_t ld, int64_t ignore_index,
+                                                          float* row_loss, float* row_max,
+                                                          float* row_tgt, int* bad_target) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  using PK = Packed<DT>;
+  constexpr int VEC = E::kVec;
+  constexpr int U = 4;
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xrow = reinterpret_cast<const T*>(logits) + row * ld;
+  const uint4* xr = reinterpret_cast<const uint4*>(xrow);
+  const int nvi = (int)(vocab / VEC);
+  const int bd = blockDim.x;
+  int64_t tg = 0;
+  if (threadIdx.x == 0) tg = targets[row];
+  float m = -INFINITY, s = 0.f;
+  for (int v0 = threadIdx.x; v0 < nvi; v0 += U * bd) {
+    uint4 r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v0 + u * bd < nvi) r[u] = __ldcs(xr + v0 + u * bd);
+    auto pm = PK::neg_inf();
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (v0 + u * bd < nvi) PK::max4(r[u], pm);
+    const float cm = PK::init_m(pm);
+    if (cm > m) {
+      s = (m == -INFINITY) ? 0.f : s * sm100::ex2_approx((m - cm) * kLog2e);
+      m = cm;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (v0 + u * bd < nvi) {
+        float f[VEC];
+        PK::widen(r[u], f);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) s += sm100::ex2_approx((f[j] - m) * kLog2e);
+      }
+    }
+  }
+  const float gm = block_max(m, red);
+  const float gs =
+      block_sum(m == -INFINITY ? 0.f : s * sm100::ex2_approx((m - gm) * kLog2e), red);
+  if (threadIdx.x == 0) {
+    float loss, tl;
+    if (tg == ignore_index) {
+      loss = 0.f;
+      tl = NAN;
+    } else if (tg < 0 || tg >= vocab) {
+      loss = NAN;
+      tl = NAN;
+      if (bad_target) atomicExch(bad_target, 1);
+    } else {
+      tl = E::to_f(xrow[tg]);
+      loss = (gm + logf(gs)) - tl;
+    }
+    row_loss[row] = loss;
+    if (row_max) row_max[row] = gm;
+    if (row_tgt) row_tgt[row] = tl;
+  }
+}
+
 template <int ODT>
 __global__ void __launch_bounds__(1024) xent_final_kernel(const float* row_loss,
                                                           const int64_t* targets, int64_t rows,
@@ -319,6 +392,13 @@ extern "C" int ak_cross_entropy_rows(const void* logits, const int64_t* targets,
   if (rows == 0) return AK_OK;
   AK_REQUIRE(logits && targets && row_loss, AK_ERR_ARG, "null tensor pointer");
   cudaStream_t st = (cudaStream_t)stream;
+  if (vocab % 8 == 0 && ld % 8 == 0 && aligned16(logits)) {
+    AK_DISPATCH_DT(dtype, xent_stream_kernel,
+                   <<<(unsigned)rows, 256, 0, st>>>(logits, targets, vocab, ld, ignore_index,
+                                                    row_loss, row_max, row_target_logit,
+                                                    bad_target))
+    return launch_status("cross_entropy_rows");
+  }
   const int threads = vocab >= 16384 ? 512 : vocab >= 2048 ? 256 : 128;
   AK_DISPATCH_DT(dtype, xent_row_kernel,
                  <<<(unsigned)rows, threads, 0, st>>>(logits, targets, rows, vocab, ld,

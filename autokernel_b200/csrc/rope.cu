@@ -7,9 +7,10 @@
 // (cs_div = 1, cs_rows = S) and model-style x [B,S,H,D] with cos [S,1,D/2]
 // (cs_div = H).  cos/sin may be the dtype of x or fp32.
 //
-// Each thread handles one 16-byte vector of x (4 pairs in 16-bit types, 2 in
-// fp32) and the matching cos/sin pieces, so x is read once and y written once
-// with 128-bit accesses; cos/sin (1 MB at S=4096) stay in L2.  Arithmetic is
+// Each thread handles 16-byte vectors of x (4 pairs in 16-bit types, 2 in
+// fp32) and the matching cos/sin pieces, four vectors in flight at a time, so x
+// is read once and y written once with 128-bit accesses; cos/sin (1 MB at
+// S=4096) stay in L2.  Arithmetic is
 // fp32 with a single rounding at the store.
 #include "ak_common.cuh"
 
@@ -21,6 +22,7 @@ struct RopeArgs {
   const void* sin;
   void* y;
   int64_t rows, d, cs_div, cs_rows;
+  FastDiv f_vpr, f_div, f_rows;  // 32-bit index path (total vectors < 2^31)
 };
 
 template <int CDT, int N>
@@ -46,26 +48,94 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(RopeArgs a) {
   using CT = typename Elem<CDT>::T;
   constexpr int VEC = E::kVec;
   constexpr int P = VEC / 2;  // pairs per vector
+  constexpr int U = 4;        // vectors in flight per thread
   const int64_t vpr = a.d / VEC;  // vectors per row
   const int64_t total = a.rows * vpr;
   const int64_t half = a.d / 2;
-  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
-       g += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = g / vpr;
-    const int64_t v = g - row * vpr;
-    const int64_t crow = (row / a.cs_div) % a.cs_rows;
-    float xf[VEC], c[P], s[P], o[VEC];
-    load_vec_stream<DT>(reinterpret_cast<const T*>(a.x) + g * VEC, xf);
-    const int64_t coff = crow * half + v * P;
-    load_cs<CDT, P>(reinterpret_cast<const CT*>(a.cos) + coff, c);
-    load_cs<CDT, P>(reinterpret_cast<const CT*>(a.sin) + coff, s);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t g0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g0 < total; g0 += U * stride) {
+    uint4 xr[U];
+    float c[U][P], s[U][P];
 #pragma unroll
-    for (int p = 0; p < P; ++p) {
-      const float x1 = xf[2 * p], x2 = xf[2 * p + 1];
-      o[2 * p] = fmaf(x1, c[p], -x2 * s[p]);
-      o[2 * p + 1] = fmaf(x1, s[p], x2 * c[p]);
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = g0 + u * stride;
+      if (g < total) xr[u] = __ldcs(reinterpret_cast<const uint4*>(a.x) + g);
     }
-    store_vec<DT>(reinterpret_cast<T*>(a.y) + g * VEC, o);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = g0 + u * stride;
+      if (g < total) {
+        const int64_t row = g / vpr;
+        const int64_t v = g - row * vpr;
+        const int64_t coff = ((row / a.cs_div) % a.cs_rows) * half + v * P;
+        load_cs<CDT, P>(reinterpret_cast<const CT*>(a.cos) + coff, c[u]);
+        load_cs<CDT, P>(reinterpret_cast<const CT*>(a.sin) + coff, s[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = g0 + u * stride;
+      if (g >= total) continue;
+      const T* e = reinterpret_cast<const T*>(&xr[u]);
+      float o[VEC];
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        const float x1 = E::to_f(e[2 * q]), x2 = E::to_f(e[2 * q + 1]);
+        o[2 * q] = fmaf(x1, c[u][q], -x2 * s[u][q]);
+        o[2 * q + 1] = fmaf(x1, s[u][q], x2 * c[u][q]);
+      }
+      store_vec<DT>(reinterpret_cast<T*>(a.y) + g * VEC, o);
+    }
+  }
+}
+
+// Same as rope_vec_kernel with 32-bit indices and multiply-high divisions:
+// the 64-bit divisions above cost more issue slots than the memory traffic
+// leaves.  Used when rows * D / VEC < 2^31.
+template <int DT, int CDT>
+__global__ void __launch_bounds__(256) rope_vec32_kernel(RopeArgs a) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  using CT = typename Elem<CDT>::T;
+  constexpr int VEC = E::kVec;
+  constexpr int P = VEC / 2;
+  constexpr int U = 4;
+  const uint32_t total = (uint32_t)(a.rows * (a.d / VEC));
+  const uint32_t half = (uint32_t)(a.d / 2);
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t g0 = blockIdx.x * blockDim.x + threadIdx.x; g0 < total; g0 += U * stride) {
+    uint4 xr[U];
+    float c[U][P], s[U][P];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t g = g0 + u * stride;
+      if (g < total) xr[u] = __ldcs(reinterpret_cast<const uint4*>(a.x) + g);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t g = g0 + u * stride;
+      if (g < total) {
+        const uint32_t row = a.f_vpr.div(g);
+        const uint32_t v = g - row * a.f_vpr.d;
+        const uint32_t coff = a.f_rows.mod(a.f_div.div(row)) * half + v * P;
+        load_cs<CDT, P>(reinterpret_cast<const CT*>(a.cos) + coff, c[u]);
+        load_cs<CDT, P>(reinterpret_cast<const CT*>(a.sin) + coff, s[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t g = g0 + u * stride;
+      if (g >= total) continue;
+      const T* e = reinterpret_cast<const T*>(&xr[u]);
+      float o[VEC];
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        const float x1 = E::to_f(e[2 * q]), x2 = E::to_f(e[2 * q + 1]);
+        o[2 * q] = fmaf(x1, c[u][q], -x2 * s[u][q]);
+        o[2 * q + 1] = fmaf(x1, s[u][q], x2 * c[u][q]);
+      }
+      store_vec<DT>(reinterpret_cast<T*>(a.y) + (size_t)g * VEC, o);
+    }
   }
 }
 
@@ -104,7 +174,15 @@ static int run_rope(const RopeArgs& a, cudaStream_t st) {
   const int64_t cap = (int64_t)sms * 16;  // grid-stride beyond 16 CTAs per SM
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  if (vec) rope_vec_kernel<DT, CDT><<<(unsigned)blocks, 256, 0, st>>>(a);
+  const bool small = units < (1LL << 31) && a.rows < (1LL << 31) && a.cs_div < (1LL << 31) &&
+                     a.cs_rows < (1LL << 31);
+  if (vec && small) {
+    RopeArgs b = a;
+    b.f_vpr = FastDiv((uint32_t)(a.d / VEC));
+    b.f_div = FastDiv((uint32_t)a.cs_div);
+    b.f_rows = FastDiv((uint32_t)a.cs_rows);
+    rope_vec32_kernel<DT, CDT><<<(unsigned)blocks, 256, 0, st>>>(b);
+  } else if (vec) rope_vec_kernel<DT, CDT><<<(unsigned)blocks, 256, 0, st>>>(a);
   else rope_scalar_kernel<DT, CDT><<<(unsigned)blocks, 256, 0, st>>>(a);
   return launch_status("rotary_embedding");
 }
@@ -124,7 +202,7 @@ extern "C" int ak_rotary_embedding(const void* x, const void* cos, const void* s
   AK_REQUIRE(rows >= 0 && cs_div >= 1 && cs_rows >= 1, AK_ERR_SHAPE, "bad rope broadcast");
   if (rows == 0) return AK_OK;
   AK_REQUIRE(x && y && cos && sin, AK_ERR_ARG, "null tensor pointer");
-  RopeArgs a{x, cos, sin, y, rows, head_dim, cs_div, cs_rows};
+  RopeArgs a{x, cos, sin, y, rows, head_dim, cs_div, cs_rows, FastDiv(), FastDiv(), FastDiv()};
   cudaStream_t st = (cudaStream_t)stream;
   if (cs_dtype == AK_F32) {
     switch (dtype) {

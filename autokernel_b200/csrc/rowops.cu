@@ -17,6 +17,7 @@
 // whose rows do not start on 16-byte boundaries) and rows wider than the
 // register budget; it re-reads the row from L2.
 #include "ak_common.cuh"
+#include "rowring.cuh"
 
 namespace ak {
 
@@ -224,6 +225,14 @@ static void launch_reg(const RowArgs& a, int G, cudaStream_t s) {
 template <int DT, int OP>
 static int run_rowop(const RowArgs& a, cudaStream_t s) {
   constexpr int VEC = Elem<DT>::kVec;
+  if (OP == OP_SOFTMAX) {
+    // long aligned rows: persistent TMA-staged ring (rowring.cu)
+    RingArgs ra{};
+    ra.x = a.x; ra.y = a.y;
+    ra.rows = a.rows; ra.cols = a.cols; ra.ldx = a.ldx; ra.ldy = a.ldy;
+    const int rc = ring_rowop(RING_SOFTMAX, DT, ra, s);
+    if (rc != 1) return rc;
+  }
   const bool vec_ok = (a.cols % VEC == 0) && (a.ldx % VEC == 0) && (a.ldy % VEC == 0) &&
                       aligned16(a.x) && aligned16(a.y) &&
                       (OP == OP_SOFTMAX || aligned16(a.w)) && (OP != OP_LN || aligned16(a.b));

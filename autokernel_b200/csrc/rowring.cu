@@ -1,0 +1,268 @@
+// Persistent row kernels fed by a TMA bulk-copy ring in shared memory, for the
+// long rows of softmax (reference.py:15-17).
+//
+// One 512-thread CTA per SM holds a ring of S = 200 KiB / row-bytes slots (3
+// for 64 KiB rows), each filled with one row by cp.async.bulk (global ->
+// shared, completion counted on one mbarrier per slot).  The CTA is two
+// independent 256-thread groups that take alternate rows, so one group's
+// reductions and stores overlap the other's; each group refills the slot it
+// just finished with the row S ahead.  The statistics passes read the staged
+// row from shared memory, the output pass writes straight to HBM with 16-byte
+// streaming stores.  HBM traffic stays one read of x (and one write of y).
+//
+// Softmax keeps exp(x - max) in registers for the output pass, packed as half2
+// for 16-bit rows (relative error 2^-12, below the 1e-3 tolerance and under the
+// rounding of a bf16 output).  Reductions are fixed-order (warp shuffles, then
+// the group's warps in index order through shared memory and a named barrier
+// per group): deterministic.
+#include "rowring.cuh"
+#include "sm100.cuh"
+#include "packed.cuh"
+
+#include <cstdlib>
+#include <mutex>
+
+namespace ak {
+namespace ring {
+
+using namespace sm100;
+
+constexpr int THREADS = 512;
+constexpr int MAX_STAGES = 8;
+constexpr int SMEM_BUDGET = 200 * 1024;
+
+AK_D void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+AK_D void named_bar(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+
+// Sum / max over the TPR threads of group g (deterministic order).
+template <int TPR>
+AK_D float group_sum(float v, float* red, int g, int t) {
+  v = warp_sum(v);
+  if constexpr (TPR == 32) {
+    return v;
+  } else {
+    constexpr int NW = TPR / 32;
+    if ((t & 31) == 0) red[g * 16 + (t >> 5)] = v;
+    named_bar(1 + g, TPR);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) s += red[g * 16 + i];
+    named_bar(1 + g, TPR);
+    return s;
+  }
+}
+template <int TPR>
+AK_D float group_max(float v, float* red, int g, int t) {
+  v = warp_max(v);
+  if constexpr (TPR == 32) {
+    return v;
+  } else {
+    constexpr int NW = TPR / 32;
+    if ((t & 31) == 0) red[g * 16 + (t >> 5)] = v;
+    named_bar(1 + g, TPR);
+    float s = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) s = fmaxf(s, red[g * 16 + i]);
+    named_bar(1 + g, TPR);
+    return s;
+  }
+}
+
+struct Launch {
+  int stages;
+  int stage_bytes;
+  int nvt;  // 16-byte vectors per thread per row
+};
+
+constexpr int GROUPS = 2;             // independent consumer groups per CTA
+constexpr int TPG = THREADS / GROUPS;  // threads per group (one row at a time)
+constexpr int MAX_NVT = 16;            // 16-byte vectors per thread: rows <= 64 KiB
+
+// All threads of group g vote; true only if every one passed `ok`.
+AK_D bool group_all(int ok, int g) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(ok), "r"(1 + g), "r"(TPG)
+      : "memory");
+  return r != 0;
+}
+
+template <int DT, int OP>
+__global__ void __launch_bounds__(THREADS, 1) ring_kernel(RingArgs a, Launch L) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  using PK = Packed<DT>;
+  constexpr int VEC = E::kVec;
+  // softmax keeps exp(x - max) per element: fp32, or packed half2 for 16-bit rows
+  constexpr bool HALF_EX = DT != AK_F32;
+  constexpr int EXW = HALF_EX ? VEC / 2 : VEC;  // 32-bit words per vector
+  extern __shared__ __align__(128) uint8_t ring_smem[];
+  __shared__ uint64_t full[MAX_STAGES];
+  __shared__ float red[GROUPS * 16];
+  __shared__ int abort_flag;
+  volatile int* abort_p = &abort_flag;
+
+  const int tid = threadIdx.x, g = tid / TPG, t = tid % TPG;
+  const int64_t rows = a.rows, cols = a.cols;
+  const int nvi = (int)(cols / VEC);
+  const uint32_t row_bytes = (uint32_t)(cols * sizeof(T));
+
+  // k-th row of this CTA: blockIdx.x + k * gridDim.x, staged in slot k % stages
+  auto issue = [&](int64_t k) {
+    const int64_t row = blockIdx.x + k * gridDim.x;
+    if (row >= rows) return;
+    const int s = (int)(k % L.stages);
+    mbar_expect_tx(&full[s], row_bytes);
+    bulk_load(ring_smem + (size_t)s * L.stage_bytes,
+              reinterpret_cast<const T*>(a.x) + row * a.ldx, row_bytes, &full[s]);
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < L.stages; ++s) mbar_init(&full[s], 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int s = 0; s < L.stages; ++s) issue(s);
+
+  for (int64_t k = g;; k += GROUPS) {
+    const int64_t row = blockIdx.x + k * gridDim.x;
+    if (row >= rows) break;
+    const int s = (int)(k % L.stages);
+    const int w = mbar_wait(&full[s], (uint32_t)((k / L.stages) & 1), abort_p) ? 1 : 0;
+    if (!group_all(w, g)) break;
+    const uint4* sv = reinterpret_cast<const uint4*>(ring_smem + (size_t)s * L.stage_bytes);
+
+    auto pm = PK::neg_inf();
+    for (int i = 0, v = t; i < L.nvt && v < nvi; ++i, v += TPG) PK::max4(sv[v], pm);
+    const float m = group_max<TPG>(PK::init_m(pm), red, g, t);
+    float acc = 0.f;
+    {
+      uint32_t ex[MAX_NVT][EXW];
+#pragma unroll
+      for (int i = 0; i < MAX_NVT; ++i) {
+        const int v = t + i * TPG;
+        if (i < L.nvt && v < nvi) {
+          float f[VEC];
+          PK::widen(sv[v], f);
+#pragma unroll
+          for (int j = 0; j < VEC; j += 2) {
+            const float e0 = ex2_approx((f[j] - m) * kLog2e);
+            const float e1 = ex2_approx((f[j + 1] - m) * kLog2e);
+            acc += e0 + e1;
+            if constexpr (HALF_EX) {
+              __half2 h = __floats2half2_rn(e0, e1);
+              ex[i][j / 2] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+              ex[i][j] = __float_as_uint(e0);
+              ex[i][j + 1] = __float_as_uint(e1);
+            }
+          }
+        }
+      }
+      const float inv = 1.0f / group_sum<TPG>(acc, red, g, t);
+      uint4* yv = reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.y) + row * a.ldy);
+#pragma unroll
+      for (int i = 0; i < MAX_NVT; ++i) {
+        const int v = t + i * TPG;
+        if (i < L.nvt && v < nvi) {
+          float o[VEC];
+#pragma unroll
+          for (int j = 0; j < VEC; j += 2) {
+            if constexpr (HALF_EX) {
+              const float2 e = __half22float2(*reinterpret_cast<const __half2*>(&ex[i][j / 2]));
+              o[j] = e.x * inv;
+              o[j + 1] = e.y * inv;
+            } else {
+              o[j] = __uint_as_float(ex[i][j]) * inv;
+              o[j + 1] = __uint_as_float(ex[i][j + 1]) * inv;
+            }
+          }
+          __stcs(yv + v, PK::narrow(o));
+        }
+      }
+    }
+    // the group is done with slot s: refill it with this CTA's row `stages` ahead
+    named_bar(1 + g, TPG);
+    if (t == 0) {
+      fence_proxy_async();
+      issue(k + L.stages);
+    }
+  }
+}
+
+template <int DT, int OP>
+static int dispatch(const RingArgs& a, cudaStream_t st) {
+  constexpr int VEC = Elem<DT>::kVec;
+  const int esz = (int)sizeof(typename Elem<DT>::T);
+  const int64_t row_bytes = a.cols * esz;
+  // rows of 16-64 KiB, 16-byte aligned: shorter rows go to the register kernels
+  if (row_bytes < 16 * 1024 || row_bytes > 64 * 1024 || row_bytes % 16) return 1;
+  if ((a.ldx * esz) % 16 || !aligned16(a.x)) return 1;
+  if (!aligned16(a.y) || (a.ldy * esz) % 16) return 1;
+  Launch L;
+  L.stage_bytes = (int)row_bytes;
+  L.stages = SMEM_BUDGET / L.stage_bytes;
+  if (L.stages > MAX_STAGES) L.stages = MAX_STAGES;
+  if (L.stages < 3) return 1;
+  L.nvt = (int)((a.cols / VEC + TPG - 1) / TPG);
+  if (L.nvt > MAX_NVT) return 1;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(ring_kernel<DT, OP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               SMEM_BUDGET);
+  });
+  AK_REQUIRE(err == cudaSuccess, AK_ERR_LAUNCH, "ring smem attribute: %s", cudaGetErrorString(err));
+  int grid = device_info().sm_count;
+  if (grid > a.rows) grid = (int)a.rows;
+  ring_kernel<DT, OP><<<grid, THREADS, L.stages * L.stage_bytes, st>>>(a, L);
+  return launch_status("ring_rowop");
+}
+
+template <int OP>
+static int by_dtype(int dtype, const RingArgs& a, cudaStream_t st) {
+  switch (dtype) {
+    case AK_F32: return dispatch<AK_F32, OP>(a, st);
+    case AK_F16: return dispatch<AK_F16, OP>(a, st);
+    case AK_BF16: return dispatch<AK_BF16, OP>(a, st);
+  }
+  return 1;
+}
+
+}  // namespace ring
+
+static int g_ring_disabled = [] {
+  const char* e = getenv("AK_DISABLE_RING");
+  return (e && e[0] == '1') ? 1 : 0;
+}();
+
+int ring_rowop(int op, int dtype, const RingArgs& a, cudaStream_t s) {
+  if (g_ring_disabled || a.rows == 0 || device_info().cc_major < 9) return 1;
+  // Only softmax uses the ring: RMSNorm / LayerNorm rows (8 KiB in the configs)
+  // run faster on the register-resident kernel with many CTAs per SM (measured
+  // 93% / 81% of HBM at 16384 x 4096 bf16), and cross entropy, which writes
+  // nothing per element, on the streaming kernel in reduce.cu.
+  switch (op) {
+    case RING_SOFTMAX: return ring::by_dtype<RING_SOFTMAX>(dtype, a, s);
+  }
+  return 1;
+}
+
+}  // namespace ak
