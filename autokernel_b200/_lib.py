@@ -44,6 +44,8 @@ SIGNATURES = {
     "ak_mlp_gate_up": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ak_fused_mlp": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ak_flash_attention": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _vp]),
+    "ak_flash_attention_strided": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
+                                          _vp, _vp, _vp, _vp, _i32, _f32, _i32, _vp]),
 }
 
 _lib = None
@@ -108,9 +110,19 @@ def require_cuda(*ts: torch.Tensor) -> torch.device:
     return dev
 
 
+_forced_simt = False
+
+
 def force_simt(on: bool) -> None:
     """Test hook: route contractions through the SIMT kernels."""
+    global _forced_simt
+    _forced_simt = bool(on)
     load().ak_set_force_simt(1 if on else 0)
+
+
+def forced_simt() -> bool:
+    import os
+    return _forced_simt or os.environ.get("AK_FORCE_SIMT") == "1"
 
 
 def device_status(clear: bool = True) -> int:

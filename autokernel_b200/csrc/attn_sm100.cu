@@ -2,10 +2,13 @@
 //   O = softmax(Q K^T * scale [+ causal mask]) V,  Q/O [BH, Sq, D], K/V [BH, Sk, D],
 // bf16/fp16 in, fp32 softmax statistics and accumulators, D in {64, 128}.
 //
+// Q/K/V/O may be strided views [batch, heads, seq, D] (e.g. the [B, T, H, D]
+// projection outputs of a transformer read in place); K/V may have fewer heads
+// (grouped-query attention: query head h reads key/value head h / (H / Hkv)).
 // One CTA owns two 128-row query tiles (A, B) of one (batch, head) and walks the
 // key/value sequence in 128-key blocks.  320 threads, warp-specialised:
 //   warp 0      TMA producer: Q tiles once, then a 2-stage ring of {K, V} blocks
-//               (3-D tensor maps [BH, S, D], so tails zero-fill inside a head)
+//               (4-D tensor maps [B, H, S, D], so tails zero-fill inside a head)
 //   warp 1      TMEM allocator (512 columns) + single-thread MMA issuer
 //   warps 2..5  softmax / epilogue of tile A, one thread per query row
 //   warps 6..9  softmax / epilogue of tile B
@@ -28,6 +31,8 @@
 
 #include <mutex>
 
+#include "attn.cuh"
+
 namespace ak {
 namespace attn {
 
@@ -49,7 +54,8 @@ struct Cfg {
 
 struct Params {
   void* O;
-  int Sq, Sk, BH;
+  int64_t o_sb, o_sh, o_ss;  // output strides (elements): batch, head, sequence
+  int Sq, Sk, H, rep;        // rep = query heads per key/value head
   int causal;
   float scale_log2;  // sm_scale * log2(e)
   uint32_t idesc_qk, idesc_pv;
@@ -71,7 +77,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
+  const int b = blockIdx.x / p.H, h = blockIdx.x % p.H, hk = h / p.rep;
   const int qblk = p.n_qblk - 1 - (int)blockIdx.y;  // heaviest (causal) blocks first
   const int q0 = qblk * 2 * BQ;
   // key blocks this CTA needs: all of them, or up to the diagonal of its last row
@@ -114,19 +120,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_expect_tx(&q_full, 2 * C::TILE_BYTES);
       for (int x = 0; x < 2; ++x)
         for (int c = 0; c < C::NC; ++c)
-          tma_load_3d(smem + C::Q_OFF + x * C::TILE_BYTES + c * CHUNK_BYTES, &tq, &q_full, c * 64,
-                      q0 + x * BQ, bh);
+          tma_load_4d(smem + C::Q_OFF + x * C::TILE_BYTES + c * CHUNK_BYTES, &tq, &q_full, c * 64,
+                      q0 + x * BQ, h, b);
       for (int j = 0; j < n_kv; ++j) {
         const int st = j & 1;
         if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, abort_p)) break;
         mbar_expect_tx(&k_full[st], C::TILE_BYTES);
         for (int c = 0; c < C::NC; ++c)
-          tma_load_3d(smem + C::K_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tk, &k_full[st],
-                      c * 64, j * BKV, bh);
+          tma_load_4d(smem + C::K_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tk, &k_full[st],
+                      c * 64, j * BKV, hk, b);
         mbar_expect_tx(&v_full[st], C::TILE_BYTES);
         for (int c = 0; c < C::NC; ++c)
-          tma_load_3d(smem + C::V_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tv, &v_full[st],
-                      c * 64, j * BKV, bh);
+          tma_load_4d(smem + C::V_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tv, &v_full[st],
+                      c * 64, j * BKV, hk, b);
       }
     }
   } else if (warp == 1) {
@@ -269,7 +275,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (w) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = reinterpret_cast<T*>(p.O) + ((int64_t)bh * p.Sq + qrow) * D;
+      T* orow = reinterpret_cast<T*>(p.O) + b * p.o_sb + h * p.o_sh + (int64_t)qrow * p.o_ss;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
@@ -300,31 +306,38 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 namespace attn {
 
-static bool make_tmap_3d(CUtensorMap* m, int dtype, const void* base, int S, int D, int64_t BH) {
-  uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)BH};
-  uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
-  uint32_t box[3] = {64, 128, 1};
-  return make_tmap(m, dtype, 3, base, dims, strides, box);
+// 4-D map over [batch, heads, seq, D] with arbitrary (16-byte multiple) strides,
+// innermost D contiguous; boxes of 128 rows x 64 elements.
+static bool make_tmap_4d(CUtensorMap* m, int dtype, const void* base, int64_t B, int64_t H,
+                         int S, int D, const int64_t* st) {
+  uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+  uint64_t strides[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
+  uint32_t box[4] = {64, 128, 1, 1};
+  return make_tmap(m, dtype, 4, base, dims, strides, box);
 }
 
 template <int DT, int D>
-static int launch(const void* Q, const void* K, const void* V, void* O, int64_t bh, int Sq,
-                  int Sk, int causal, float scale, cudaStream_t st) {
+static int launch(const AttnShape& a, cudaStream_t st) {
   CUtensorMap tq, tk, tv;
-  if (!make_tmap_3d(&tq, DT, Q, Sq, D, bh) || !make_tmap_3d(&tk, DT, K, Sk, D, bh) ||
-      !make_tmap_3d(&tv, DT, V, Sk, D, bh))
+  if (!make_tmap_4d(&tq, DT, a.Q, a.B, a.H, a.Sq, D, a.qs) ||
+      !make_tmap_4d(&tk, DT, a.K, a.B, a.Hkv, a.Sk, D, a.ks) ||
+      !make_tmap_4d(&tv, DT, a.V, a.B, a.Hkv, a.Sk, D, a.vs))
     return AK_ERR_LAUNCH;
   Params p;
-  p.O = O;
-  p.Sq = Sq;
-  p.Sk = Sk;
-  p.BH = (int)bh;
-  p.causal = causal;
-  p.scale_log2 = scale * 1.4426950408889634f;
+  p.O = a.O;
+  p.o_sb = a.os[0];
+  p.o_sh = a.os[1];
+  p.o_ss = a.os[2];
+  p.Sq = a.Sq;
+  p.Sk = a.Sk;
+  p.H = (int)a.H;
+  p.rep = (int)(a.H / a.Hkv);
+  p.causal = a.causal;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
   const int fmt = DT == AK_BF16 ? 1 : 0;
   p.idesc_qk = idesc_f16(fmt, BQ, BKV, false, false);
   p.idesc_pv = idesc_f16(fmt, BQ, D, false, true);
-  p.n_qblk = (Sq + 2 * BQ - 1) / (2 * BQ);
+  p.n_qblk = (a.Sq + 2 * BQ - 1) / (2 * BQ);
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
@@ -333,31 +346,37 @@ static int launch(const void* Q, const void* K, const void* V, void* O, int64_t 
   });
   AK_REQUIRE(attr == cudaSuccess, AK_ERR_LAUNCH, "attention smem attribute: %s",
              cudaGetErrorString(attr));
-  dim3 grid((unsigned)bh, (unsigned)p.n_qblk);
+  dim3 grid((unsigned)(a.B * a.H), (unsigned)p.n_qblk);
   attn_kernel<DT, D><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tq, tk, tv, p);
   return launch_status("tc_attention");
 }
 
 }  // namespace attn
 
-bool tc_attention_ok(int dtype, const void* Q, const void* K, const void* V, const void* O,
-                     int D) {
-  if (dtype != AK_F16 && dtype != AK_BF16) return false;
-  if (D != 64 && D != 128) return false;
-  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return false;
+static bool strides_ok(const int64_t* st) {
+  return st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0 && st[0] > 0 && st[1] > 0 &&
+         st[2] > 0;
+}
+
+bool tc_attention_ok(const AttnShape& a) {
+  if (a.dtype != AK_F16 && a.dtype != AK_BF16) return false;
+  if (a.D != 64 && a.D != 128) return false;
+  if (!aligned16(a.Q) || !aligned16(a.K) || !aligned16(a.V) || !aligned16(a.O)) return false;
+  if (!strides_ok(a.qs) || !strides_ok(a.ks) || !strides_ok(a.vs) || !strides_ok(a.os))
+    return false;
+  if (a.Hkv <= 0 || a.H % a.Hkv) return false;
   return device_info().cc_major == 10;
 }
 
-int tc_attention(int dtype, const void* Q, const void* K, const void* V, void* O, int64_t bh,
-                 int Sq, int Sk, int D, int causal, float scale, cudaStream_t s) {
-  AK_REQUIRE(bh <= 0x7fffffffLL, AK_ERR_SHAPE, "batch*heads too large");
-  AK_REQUIRE((Sq + 255) / 256 <= 65535, AK_ERR_SHAPE, "sequence too long for the grid");
-  if (dtype == AK_BF16) {
-    if (D == 128) return attn::launch<AK_BF16, 128>(Q, K, V, O, bh, Sq, Sk, causal, scale, s);
-    return attn::launch<AK_BF16, 64>(Q, K, V, O, bh, Sq, Sk, causal, scale, s);
+int tc_attention(const AttnShape& a, cudaStream_t s) {
+  AK_REQUIRE(a.B * a.H <= 0x7fffffffLL, AK_ERR_SHAPE, "batch*heads too large");
+  AK_REQUIRE((a.Sq + 255) / 256 <= 65535, AK_ERR_SHAPE, "sequence too long for the grid");
+  if (a.dtype == AK_BF16) {
+    if (a.D == 128) return attn::launch<AK_BF16, 128>(a, s);
+    return attn::launch<AK_BF16, 64>(a, s);
   }
-  if (D == 128) return attn::launch<AK_F16, 128>(Q, K, V, O, bh, Sq, Sk, causal, scale, s);
-  return attn::launch<AK_F16, 64>(Q, K, V, O, bh, Sq, Sk, causal, scale, s);
+  if (a.D == 128) return attn::launch<AK_F16, 128>(a, s);
+  return attn::launch<AK_F16, 64>(a, s);
 }
 
 }  // namespace ak

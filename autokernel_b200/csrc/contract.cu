@@ -4,6 +4,7 @@
 // choice depends only on dtype/shape/alignment, never on the data, so a given
 // call is bitwise reproducible.
 #include "ak_common.cuh"
+#include "attn.cuh"
 
 #include <cstdlib>
 
@@ -18,10 +19,6 @@ int simt_gemm_any(int dtype, const void* A, const void* B, const void* B2, void*
 int simt_attention_any(int dtype, const void* Q, const void* K, const void* V, void* O,
                        int64_t bh, int Sq, int Sk, int D, int causal, float scale,
                        cudaStream_t s);
-bool tc_attention_ok(int dtype, const void* Q, const void* K, const void* V, const void* O,
-                     int D);
-int tc_attention(int dtype, const void* Q, const void* K, const void* V, void* O, int64_t bh,
-                 int Sq, int Sk, int D, int causal, float scale, cudaStream_t s);
 
 // Route every contraction through the SIMT kernels: set by ak_set_force_simt()
 // or, at load time, by the environment variable AK_FORCE_SIMT=1.
@@ -91,6 +88,37 @@ extern "C" int ak_fused_mlp(const void* x, const void* w_gate, const void* w_up,
   return ak_matmul(hidden, w_down, out, M, D, H, H, H, D, 1, dtype, stream);
 }
 
+extern "C" int ak_flash_attention_strided(const void* Q, const void* K, const void* V, void* O,
+                                          int64_t B, int64_t H, int64_t Hkv, int64_t Sq,
+                                          int64_t Sk, int64_t D, const int64_t* q_strides,
+                                          const int64_t* k_strides, const int64_t* v_strides,
+                                          const int64_t* o_strides, int causal, float sm_scale,
+                                          int dtype, void* stream) {
+  AK_REQUIRE(dtype_ok(dtype), AK_ERR_DTYPE, "unsupported dtype %d", dtype);
+  AK_REQUIRE(B >= 0 && H >= 0 && Hkv > 0 && Sq >= 0 && Sk >= 0 && D > 0, AK_ERR_SHAPE,
+             "bad shape");
+  AK_REQUIRE(H % Hkv == 0, AK_ERR_SHAPE, "query heads %lld not a multiple of kv heads %lld",
+             (long long)H, (long long)Hkv);
+  AK_REQUIRE(Sq < (1LL << 31) && Sk < (1LL << 31), AK_ERR_SHAPE, "sequence too long");
+  if (B == 0 || H == 0 || Sq == 0) return AK_OK;
+  AK_REQUIRE(Sk > 0, AK_ERR_SHAPE, "attention over zero keys");
+  AK_REQUIRE(Q && K && V && O && q_strides && k_strides && v_strides && o_strides, AK_ERR_ARG,
+             "null pointer");
+  AttnShape a;
+  a.Q = Q; a.K = K; a.V = V; a.O = O;
+  a.B = B; a.H = H; a.Hkv = Hkv;
+  a.Sq = (int)Sq; a.Sk = (int)Sk; a.D = (int)D;
+  for (int i = 0; i < 3; ++i) {
+    a.qs[i] = q_strides[i]; a.ks[i] = k_strides[i];
+    a.vs[i] = v_strides[i]; a.os[i] = o_strides[i];
+  }
+  a.causal = causal; a.scale = sm_scale; a.dtype = dtype;
+  AK_REQUIRE(!g_force_simt && tc_attention_ok(a), AK_ERR_UNSUPPORTED,
+             "strided attention needs 16-bit inputs, head_dim 64 or 128 and 16-byte aligned "
+             "strides on sm_100; use ak_flash_attention on contiguous tensors");
+  return tc_attention(a, (cudaStream_t)stream);
+}
+
 extern "C" int ak_flash_attention(const void* Q, const void* K, const void* V, void* O,
                                   int64_t batch_heads, int64_t Sq, int64_t Sk, int64_t D,
                                   int causal, float sm_scale, int dtype, void* stream) {
@@ -101,9 +129,17 @@ extern "C" int ak_flash_attention(const void* Q, const void* K, const void* V, v
   AK_REQUIRE(Sk > 0, AK_ERR_SHAPE, "attention over zero keys");
   AK_REQUIRE(Q && K && V && O, AK_ERR_ARG, "null tensor pointer");
   cudaStream_t st = (cudaStream_t)stream;
-  if (!g_force_simt && tc_attention_ok(dtype, Q, K, V, O, (int)D))
-    return tc_attention(dtype, Q, K, V, O, batch_heads, (int)Sq, (int)Sk, (int)D, causal,
-                        sm_scale, st);
+  // contiguous [BH, S, D]: batch = BH, one head per batch entry
+  AttnShape a;
+  a.Q = Q; a.K = K; a.V = V; a.O = O;
+  a.B = batch_heads; a.H = 1; a.Hkv = 1;
+  a.Sq = (int)Sq; a.Sk = (int)Sk; a.D = (int)D;
+  const int64_t qst[3] = {Sq * D, Sq * D, D}, kst[3] = {Sk * D, Sk * D, D};
+  for (int i = 0; i < 3; ++i) {
+    a.qs[i] = qst[i]; a.os[i] = qst[i]; a.ks[i] = kst[i]; a.vs[i] = kst[i];
+  }
+  a.causal = causal; a.scale = sm_scale; a.dtype = dtype;
+  if (!g_force_simt && tc_attention_ok(a)) return tc_attention(a, st);
   return simt_attention_any(dtype, Q, K, V, O, batch_heads, (int)Sq, (int)Sk, (int)D, causal,
                             sm_scale, st);
 }

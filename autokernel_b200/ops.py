@@ -19,10 +19,12 @@ Python only validates arguments, allocates outputs/workspaces with torch and
 passes raw pointers plus the current CUDA stream to the C ABI.  Inputs must
 be CUDA tensors; there is no CPU path.  Non-contiguous inputs are made
 contiguous first (a copy), except that matmul accepts a transposed [N, K]
-weight view as B without copying.
+weight view as B, and attention accepts strided [B, H, S, D] views (e.g. the
+[B, T, H, D] projection outputs transposed), without copying.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -320,6 +322,47 @@ def fused_mlp(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down:
     return out.view(*x.shape[:-1], D)
 
 
+def _attn_strides(t: torch.Tensor) -> list[int] | None:
+    """[batch, head, seq] element strides of a 4-D [B, H, S, D] view usable by the strided
+    tensor-core entry (unit-stride D, 16-byte aligned rows), else None."""
+    if t.stride(3) != 1 or t.data_ptr() % 16:
+        return None
+    st = [t.stride(0), t.stride(1), t.stride(2)]
+    # a size-1 dim may carry any stride; give TMA a valid one
+    for i in range(3):
+        if t.shape[i] == 1:
+            st[i] = t.shape[2] * t.shape[3] if i < 2 else t.shape[3]
+    if any(x <= 0 or x % 8 for x in st):
+        return None
+    return st
+
+
+def attention_bhsd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bool = True,
+                   sm_scale: float | None = None, out: torch.Tensor | None = None):
+    """Tensor-core attention on 4-D views Q [B, H, Sq, D], K/V [B, Hkv, Sk, D] of any strides
+    (H a multiple of Hkv; query head h reads key/value head h // (H // Hkv)).  Returns O with
+    Q's shape, or writes it into `out` (any 4-D strided view).  Returns None if the layout is
+    not eligible for the tensor-core path (the caller falls back)."""
+    require_cuda(Q, K, V)
+    B, H, Sq, D = Q.shape
+    Hkv = K.shape[1]
+    if (Q.dtype not in (torch.float16, torch.bfloat16) or D not in (64, 128)
+            or K.shape != V.shape or K.shape[0] != B or K.shape[3] != D or H % Hkv
+            or not (Q.dtype == K.dtype == V.dtype) or _lib.forced_simt()):
+        return None
+    o = torch.empty(Q.shape, dtype=Q.dtype, device=Q.device) if out is None else out
+    st = [_attn_strides(t) for t in (Q, K, V, o)]
+    if any(x is None for x in st):
+        return None
+    if sm_scale is None:
+        sm_scale = D ** -0.5
+    arr = [(ctypes.c_int64 * 3)(*x) for x in st]
+    call("ak_flash_attention_strided", Q.data_ptr(), K.data_ptr(), V.data_ptr(), o.data_ptr(), B,
+         H, Hkv, Sq, K.shape[2], D, *[ctypes.addressof(a) for a in arr], 1 if causal else 0,
+         float(sm_scale), dtype_code(Q.dtype), stream_ptr(Q.device))
+    return o
+
+
 def flash_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: bool = True,
                     sm_scale: float | None = None) -> torch.Tensor:
     """softmax(Q K^T * scale [+ causal mask]) V (reference.py:32-42)."""
@@ -333,10 +376,16 @@ def flash_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, causal: b
         raise ValueError("head_dim of K / V must match Q")
     if sm_scale is None:
         sm_scale = D ** -0.5
-    lead = torch.broadcast_shapes(Q.shape[:-2], K.shape[:-2], V.shape[:-2])
     Sq, Sk = Q.shape[-2], K.shape[-2]
     if V.shape[-2] != Sk:
         raise ValueError("K and V sequence lengths differ")
+    if (Q.dim() == 4 and K.shape == V.shape and K.shape[0] == Q.shape[0]
+            and K.shape[1] in (1, Q.shape[1])):
+        # strided views and a single broadcast key/value head go to the tensor cores as-is
+        o = attention_bhsd(Q, K, V, causal, sm_scale)
+        if o is not None:
+            return o
+    lead = torch.broadcast_shapes(Q.shape[:-2], K.shape[:-2], V.shape[:-2])
     Qc = Q.expand(*lead, Sq, D).contiguous()
     Kc = K.expand(*lead, Sk, D).contiguous()
     Vc = V.expand(*lead, Sk, D).contiguous()

@@ -207,27 +207,90 @@ def time_compute_ops(device, world, reps: int) -> dict:
     return res
 
 
+def time_llama(device, world, batch: int = 32, seq: int = 2048, reps: int = 2) -> dict:
+    """LLaMA-7B-shape forward + next-token CE, fp16 random-init N(0, 0.02)
+    weights, batch 32 x seq 2048 split over the ranks (data parallel, 32 / N sequences each),
+    loss mean all-reduced.  tok/s = 65,536 tokens / max-over-ranks time per forward."""
+    from autokernel_b200 import llama as L, shard
+    cfg = L.LLAMA_7B
+    m = L.LlamaB200(cfg, L.LlamaB200.random_weights(cfg, device, dtype=torch.float16, seed=0))
+    local = batch // world
+    g = torch.Generator(device=device).manual_seed(100 + (dist.get_rank() if world > 1 else 0))
+    tokens = torch.randint(0, cfg.vocab_size, (local, seq), device=device, generator=g)
+    loss = m.loss(tokens)
+    torch.cuda.synchronize()
+    barrier(world, device)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        loss = m.loss(tokens)
+    b.record()
+    torch.cuda.synchronize()
+    ms = shard.max_over_ranks(a.elapsed_time(b) / reps, device=device)
+    flops = L.model_flops(cfg, batch, seq)
+    tf = flops / world / (ms * 1e-3) / 1e12
+    out = {"tok/s": batch * seq / (ms * 1e-3), "ms_per_fwd": ms, "loss": float(loss.float()),
+           "TFLOP/s_per_gpu": tf, "frac_tensor": tf / peaks()["bf16_tflops_sustained"],
+           "peak_used": "bf16_tflops_sustained (measured)",
+           "config": "32 layers, d 4096, 32 heads x 128 (MHA), ffn 11008, vocab 32000, fp16, "
+                     f"batch {batch} x seq {seq}, dp{world}"}
+    del m, tokens
+    torch.cuda.empty_cache()
+    return out
+
+
 def e2e_sweep(d, device, world, steps: int) -> dict:
     """Same workload through the public API with inputs in pinned host memory: every step
-    copies the inputs host->device, runs the ops and copies every output back."""
+    copies the inputs host->device, runs the ops and copies every output back.  Copies run on
+    their own streams (one per PCIe direction) ordered by events, so each operator starts as
+    soon as its own inputs have landed and its outputs travel back while later inputs are
+    still arriving; the step ends when the last output is on the host."""
     from autokernel_b200 import ops, shard
-    keys = ["sm_x", "ln_x", "ln_w", "ln_b", "q", "k", "cos", "sin", "red_x"]
-    host = {k: torch.empty(d[k].shape, dtype=d[k].dtype, pin_memory=True) for k in keys}
-    for k in keys:
+    order = [("rope", ["q", "k", "cos", "sin"]), ("softmax", ["sm_x"]),
+             ("layernorm", ["ln_x", "ln_w", "ln_b"]), ("reduce", ["red_x"])]
+    host = {k: torch.empty(d[k].shape, dtype=d[k].dtype, pin_memory=True)
+            for _, ks in order for k in ks}
+    for k in host:
         host[k].copy_(d[k])
-    out_host = {"sm": torch.empty(d["sm_x"].shape, dtype=d["sm_x"].dtype, pin_memory=True),
-                "ln": torch.empty(d["ln_x"].shape, dtype=d["ln_x"].dtype, pin_memory=True),
-                "q": torch.empty(d["q"].shape, dtype=d["q"].dtype, pin_memory=True),
+    out_host = {"q": torch.empty(d["q"].shape, dtype=d["q"].dtype, pin_memory=True),
                 "k": torch.empty(d["k"].shape, dtype=d["k"].dtype, pin_memory=True),
+                "sm": torch.empty(d["sm_x"].shape, dtype=d["sm_x"].dtype, pin_memory=True),
+                "ln": torch.empty(d["ln_x"].shape, dtype=d["ln_x"].dtype, pin_memory=True),
                 "sum": torch.empty((), dtype=torch.float32, pin_memory=True)}
     h2d = sum(h.numel() * h.element_size() for h in host.values())
     d2h = sum(h.numel() * h.element_size() for h in out_host.values())
+    comp = torch.cuda.current_stream(device)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+    def run(name, dd):
+        if name == "rope":
+            return {"q": ops.rotary_embedding(dd["q"], dd["cos"], dd["sin"]),
+                    "k": ops.rotary_embedding(dd["k"], dd["cos"], dd["sin"])}
+        if name == "softmax":
+            return {"sm": ops.softmax(dd["sm_x"])}
+        if name == "layernorm":
+            return {"ln": ops.layernorm(dd["ln_x"], dd["ln_w"], dd["ln_b"], 1e-5)}
+        return {"sum": shard.reduce_sum_sharded(dd["red_x"], out_dtype=torch.float32)}
 
     def step():
-        dd = {k: host[k].to(device, non_blocking=True) for k in keys}
-        o = run_sweep_step(dd)
-        for k in out_host:
-            out_host[k].copy_(o[k], non_blocking=True)
+        keep = []
+        s_in.wait_stream(comp)  # no copy of this step starts before the step does
+        for name, ks in order:
+            with torch.cuda.stream(s_in):
+                dd = {k: host[k].to(device, non_blocking=True) for k in ks}
+            comp.wait_event(s_in.record_event())
+            for t in dd.values():
+                t.record_stream(comp)
+            o = run(name, dd)
+            s_out.wait_event(comp.record_event())
+            with torch.cuda.stream(s_out):
+                for k, t in o.items():
+                    t.record_stream(s_out)
+                    out_host[k].copy_(t, non_blocking=True)
+            keep.append((dd, o))
+        comp.wait_stream(s_out)
+        return keep
 
     step()
     torch.cuda.synchronize()
@@ -294,6 +357,12 @@ def ours(args):
     ops_res = None
     if not args.no_ops and rank == 0:
         ops_res = time_compute_ops(device, world, args.op_reps)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    if not args.no_llama:  # data parallel over all ranks
+        llama_res = time_llama(device, world)
+        if rank == 0:
+            ops_res = {**(ops_res or {}), "llama7b_fwd_ce": llama_res}
     cpu = None
     if not args.no_cpu and rank == 0 and world == 1:
         cpu = cpu_baseline(args.cpu_seconds)
@@ -444,6 +513,7 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-ops", action="store_true", help="skip the GEMM/MLP/attention/CE/RMSNorm lines")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-llama", action="store_true", help="skip the LLaMA-7B forward line")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--scale", type=float, default=1.0,
                     help="shrink the sweep's leading dims (profiling captures only; the bench "

@@ -172,6 +172,20 @@ AK_API int ak_flash_attention(const void* Q, const void* K, const void* V, void*
                        int64_t batch_heads, int64_t Sq, int64_t Sk, int64_t D, int causal,
                        float sm_scale, int dtype, void* stream);
 
+/* Attention on strided views: Q/O [B, H, Sq, D], K/V [B, Hkv, Sk, D] given by element
+ * strides {batch, head, seq} (last dim contiguous), so [B, T, H, D] projection outputs are read
+ * and written in place.  Query head h uses key/value head h / (H / Hkv) (grouped-query
+ * attention).  Tensor-core path only: 16-bit dtypes, D in {64, 128}, strides multiples of 8
+ * elements; otherwise AK_ERR_UNSUPPORTED.  Same math as ak_flash_attention
+ * (kernels/flash_attention.py:130, reference.py:32-42; the GQA head mapping follows
+ * models/llama_7b.py:78-80 repeat_interleave). */
+AK_API int ak_flash_attention_strided(const void* Q, const void* K, const void* V, void* O,
+                                      int64_t B, int64_t H, int64_t Hkv, int64_t Sq, int64_t Sk,
+                                      int64_t D, const int64_t* q_strides,
+                                      const int64_t* k_strides, const int64_t* v_strides,
+                                      const int64_t* o_strides, int causal, float sm_scale,
+                                      int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

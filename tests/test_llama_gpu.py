@@ -1,0 +1,60 @@
+"""LLaMA forward on the B200 kernels vs the float64 model oracle (oracle/llama_f64.py, itself
+pinned to AutoKernel's models/llama_7b.py by tests/golden/llama_tiny.pt)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle import llama_f64
+from parity import check
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(sd, cfg, dtype):
+    from autokernel_b200.llama import LlamaB200, LlamaConfig
+    c = LlamaConfig(vocab_size=cfg["vocab_size"], dim=cfg["dim"], n_layers=cfg["n_layers"],
+                    n_heads=cfg["n_heads"], n_kv_heads=cfg["n_kv_heads"], hidden_dim=cfg["hidden_dim"])
+    return LlamaB200.from_state_dict(sd, c, device="cuda", dtype=dtype)
+
+
+def _oracle_logits(m, cfg, tokens):
+    # the oracle runs on the same (rounded) weights the GPU model holds
+    sd = {k: v.double().cpu().numpy() for k, v in m.w.items()}
+    return llama_f64.forward(sd, tokens.numpy(), cfg["n_heads"], cfg["n_kv_heads"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_reference_weights_tiny(dtype):
+    """The reference tiny LlamaModel's own state_dict runs unchanged (head_dim 32: SIMT attention)."""
+    g = torch.load(GOLDEN / "llama_tiny.pt", weights_only=False)
+    m = _model(g["state_dict"], g["cfg"], dtype)
+    logits = m(g["tokens"].cuda())
+    check(logits, _oracle_logits(m, g["cfg"], g["tokens"]), "matmul", "llama tiny", scale_tol=2.0)
+
+
+@pytest.mark.parametrize("n_kv", [4, 1])
+def test_tensor_core_attention_config(n_kv):
+    """head_dim 128: projections, RoPE and attention all take the tensor-core paths."""
+    from autokernel_b200.llama import LlamaB200, LlamaConfig
+    cfg = dict(vocab_size=512, dim=512, n_layers=2, n_heads=4, n_kv_heads=n_kv, hidden_dim=1024)
+    c = LlamaConfig(**cfg)
+    m = LlamaB200(c, LlamaB200.random_weights(c, "cuda", dtype=torch.bfloat16, seed=3, std=0.05))
+    tokens = torch.randint(0, 512, (2, 320), generator=torch.Generator().manual_seed(4))
+    logits = m(tokens.cuda())
+    ref = _oracle_logits(m, cfg, tokens)
+    check(logits, ref, "matmul", "llama tc", scale_tol=2.0)
+    loss = m.loss(tokens.cuda())
+    e = llama_f64.next_token_loss(ref, tokens.numpy())
+    assert abs(float(loss.float()) - e) <= 2e-2 * max(1.0, abs(e))
+
+
+def test_forward_is_deterministic():
+    from autokernel_b200.llama import LlamaB200, LlamaConfig
+    c = LlamaConfig(vocab_size=256, dim=256, n_layers=2, n_heads=2, n_kv_heads=2, hidden_dim=512)
+    m = LlamaB200(c, LlamaB200.random_weights(c, "cuda", seed=1))
+    t = torch.randint(0, 256, (2, 200), device="cuda")
+    a, b = m(t), m(t)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)

@@ -326,3 +326,36 @@ def test_huge_magnitude_rows(op, cols):
         y = ops().cross_entropy(xd, t.to(DEV))
         e = ref_f64.cross_entropy(to_np(x), t.numpy())
         assert abs(float(y.float()) - e) <= 2e-2 * (1 + abs(e)) + 1e28, (float(y), e)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("B,T,H,Hkv,D,causal", [(2, 300, 4, 4, 128, True), (1, 256, 8, 2, 64, True),
+                                                (2, 130, 4, 1, 128, False), (1, 512, 32, 8, 128, True)])
+def test_attention_strided_gqa(dt, B, T, H, Hkv, D, causal):
+    """[B, T, H, D] projection outputs read in place; key/value head h // (H // Hkv)."""
+    r = _gen(T + H)
+    q = r(B, T, H, D).to(DTS[dt])
+    k = r(B, T, Hkv, D).to(DTS[dt])
+    v = r(B, T, Hkv, D).to(DTS[dt])
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    out = torch.empty(B, T, H, D, dtype=DTS[dt], device=DEV)
+    o = ops().attention_bhsd(qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2), causal,
+                             out=out.transpose(1, 2))
+    assert o is not None
+    rep = H // Hkv
+    Qn = to_np(q).transpose(0, 2, 1, 3)
+    Kn = np.repeat(to_np(k).transpose(0, 2, 1, 3), rep, axis=1)
+    Vn = np.repeat(to_np(v).transpose(0, 2, 1, 3), rep, axis=1)
+    e = ref_f64.attention(Qn, Kn, Vn, causal).transpose(0, 2, 1, 3)
+    check(out, e, "flash_attention", f"gqa {B}x{T}x{H}/{Hkv}x{D}")
+
+
+def test_flash_attention_noncontiguous_inputs():
+    """ops.flash_attention on transposed views takes the strided path, same result."""
+    r = _gen(3)
+    q, k, v = (r(1, 200, 4, 64).to(torch.bfloat16).to(DEV) for _ in range(3))
+    o1 = ops().flash_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+    o2 = ops().flash_attention(q.transpose(1, 2).contiguous(), k.transpose(1, 2).contiguous(),
+                               v.transpose(1, 2).contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)

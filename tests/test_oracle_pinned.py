@@ -87,3 +87,15 @@ def test_f64_oracle_matches_reference_fp32(op):
         tol = 2e-5 if op in ("flash_attention", "fused_mlp", "matmul") else 1e-5
         err = np.abs(got[finite] - ref[finite]).max() if finite.any() else 0.0
         assert err <= tol * scale, f"{case['name']}: max err {err:.3e}"
+
+
+def test_llama_oracle_matches_reference_model():
+    """oracle/llama_f64.py reproduces the reference LlamaModel's fp32 logits (golden fixture)."""
+    from conftest import GOLDEN
+    from oracle import llama_f64
+    g = torch.load(GOLDEN / "llama_tiny.pt", weights_only=False)
+    cfg = g["cfg"]
+    sd = {k: v.double().numpy() for k, v in g["state_dict"].items()}
+    got = llama_f64.forward(sd, g["tokens"].numpy(), cfg["n_heads"], cfg["n_kv_heads"])
+    ref = g["logits"].double().numpy()
+    assert np.abs(got - ref).max() <= 1e-4 * max(1.0, np.abs(ref).max())
