@@ -216,26 +216,26 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (c * 32 + i < kmax) bmax = fmaxf(bmax, __uint_as_float(r[i]));
       }
       bmax *= p.scale_log2;
-      // lazy rescale: move the reference max only when it grows by more than 8
+      // lazy rescale: move the reference max only when it grows by more than 8.  The
+      // decision is per row (lane); the TMEM rescale of O is warp-collective, so the whole
+      // warp runs it whenever any lane needs it, with alpha = 1 for the others.
+      float alpha = 1.f;
       if (bmax > m_ref + 8.f) {
-        const float m_new = bmax;
-        if (j > 0 && m_ref != -INFINITY) {
-          const float alpha = ex2_approx(m_ref - m_new);
-          l *= alpha;
+        if (j > 0 && m_ref != -INFINITY) alpha = ex2_approx(m_ref - bmax);
+        m_ref = bmax;
+      }
+      l *= alpha;
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(t_o + c * 32, r);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_o + c * 32, r);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(t_o + c * 32, r);
-          }
-          tmem_wait_st();
-        } else if (j > 0) {
-          // O holds only zeros from fully masked blocks; nothing to rescale
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(t_o + c * 32, r);
         }
-        m_ref = m_new;
+        tmem_wait_st();
       }
       // pass 2: P = exp2(s * scale_log2 - m_ref), packed in pairs over S columns [0, 64)
       float bsum = 0.f;

@@ -359,3 +359,24 @@ def test_flash_attention_noncontiguous_inputs():
                                v.transpose(1, 2).contiguous())
     torch.cuda.synchronize()
     assert torch.equal(o1, o2)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("case", ["q_is_k", "rising_keys"])
+def test_attention_row_max_jumps(dt, case):
+    """Rows whose running max grows by a lot in a later key block (self-similar queries and
+    keys put the largest score on the diagonal; growing key norms push it to the last block).
+    This exercises the rescale of the TMEM accumulator for some rows of a warp and not others."""
+    r = _gen(41)
+    B, H, S, D = 2, 4, 640, 128
+    q = r(B, H, S, D)
+    if case == "q_is_k":
+        k = q.clone()
+    else:
+        k = r(B, H, S, D) * torch.linspace(0.2, 3.0, S)[None, None, :, None]
+    v = r(B, H, S, D)
+    q, k, v = (t.to(DTS[dt]) for t in (q, k, v))
+    y = ops().flash_attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=True)
+    check(y, ref_f64.attention(to_np(q), to_np(k), to_np(v), True), "flash_attention", case)
+    from autokernel_b200 import _lib
+    assert _lib.device_status() == 0
