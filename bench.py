@@ -314,6 +314,9 @@ def ours(args):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
+        # rank 0's stdout must carry only the JSON line; NCCL's version banner goes away
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", device_id=device)
     pk = peaks()
     d = W.sweep_inputs(device, seed=rank, scale=args.scale)
