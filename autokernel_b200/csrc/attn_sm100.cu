@@ -204,17 +204,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       // keys < kmax are visible to this row
       int kmax = p.Sk - k0;
       if (p.causal) kmax = min(kmax, qrow - k0 + 1);
-      // pass 1: row max of this block
+      // The row's 128 scores come out of TMEM once (four loads, one wait) and stay in
+      // registers for both the max and the exponentials.
+      uint32_t r[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r + c * 32);
+      tmem_wait_ld();
+      // no per-element masks when every row of the warp sees the whole block
+      const bool full = __all_sync(0xffffffffu, kmax >= BKV);
+      if (!full) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= kmax) r[i] = __float_as_uint(-INFINITY);
+      }
       float bmax = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_s + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i < kmax) bmax = fmaxf(bmax, __uint_as_float(r[i]));
-      }
+      for (int i = 0; i < 128; ++i) bmax = fmaxf(bmax, __uint_as_float(r[i]));
       bmax *= p.scale_log2;
       // lazy rescale: move the reference max only when it grows by more than 8.  The
       // decision is per row (lane); the TMEM rescale of O is warp-collective, so the whole
@@ -228,29 +233,26 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_o + c * 32, r);
+          uint32_t o[32];
+          tmem_ld32(t_o + c * 32, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(t_o + c * 32, r);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_o + c * 32, o);
         }
         tmem_wait_st();
       }
-      // pass 2: P = exp2(s * scale_log2 - m_ref), packed in pairs over S columns [0, 64)
+      // P = exp2(s * scale_log2 - m_ref) (masked scores are -inf -> 0), packed in pairs
+      // over S columns [0, 64)
+      const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // fully masked row: all P = 0
       float bsum = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t r[32], pk[16];
-        tmem_ld32(t_s + c * 32, r);
-        tmem_wait_ld();
+        uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int k = c * 32 + 2 * i;
-          float a = (k < kmax && m_ref != -INFINITY)
-                        ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), p.scale_log2, -m_ref)) : 0.f;
-          float b = (k + 1 < kmax && m_ref != -INFINITY)
-                        ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), p.scale_log2, -m_ref)) : 0.f;
+          const float a = ex2_approx(fmaf(__uint_as_float(r[c * 32 + 2 * i]), p.scale_log2, -mr));
+          const float b = ex2_approx(fmaf(__uint_as_float(r[c * 32 + 2 * i + 1]), p.scale_log2, -mr));
           bsum += a + b;
           if constexpr (DT == AK_BF16) {
             __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
