@@ -182,7 +182,7 @@ def time_compute_ops(device, world, reps: int) -> dict:
         A, B = W.gemm_inputs(M, N, K, device)
         t = timeit(lambda: ops.matmul(A, B), n=max(3, reps // 4))
         tf = 2.0 * M * N * K / t / 1e12
-        res[f"matmul_bf16_{M}x{N}x{K}"] = {"TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "ms": t * 1e3}
+        res[f"matmul_bf16_{M}x{N}x{K}"] = {"TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "frac_tensor_sustained": tf / pk["bf16_tflops_sustained"], "ms": t * 1e3}
         del A, B
     torch.cuda.empty_cache()
     # fused MLP
@@ -193,7 +193,7 @@ def time_compute_ops(device, world, reps: int) -> dict:
     wd = (torch.randn(m["D"], m["H"], device=device, generator=g) * 0.02).bfloat16()
     t = timeit(lambda: ops.fused_mlp(xm, wg, wu, wd), n=max(3, reps // 4))
     tf = 6.0 * m["M"] * m["D"] * m["H"] / t / 1e12
-    res["fused_mlp_bf16_16384x4096x11008"] = {"TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "ms": t * 1e3}
+    res["fused_mlp_bf16_16384x4096x11008"] = {"TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "frac_tensor_sustained": tf / pk["bf16_tflops_sustained"], "ms": t * 1e3}
     del xm, wg, wu, wd
     torch.cuda.empty_cache()
     # causal attention
@@ -201,7 +201,7 @@ def time_compute_ops(device, world, reps: int) -> dict:
     Q, K_, V = (torch.randn(a["B"], a["H"], a["S"], a["D"], device=device, generator=g).bfloat16() for _ in range(3))
     t = timeit(lambda: ops.flash_attention(Q, K_, V, causal=True), n=max(2, reps // 8), warm=1)
     tf = W.attn_flops(a["B"], a["H"], a["S"], a["D"]) / t / 1e12
-    res["flash_attention_bf16_causal_8x32x4096x128"] = {"TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "ms": t * 1e3}
+    res["flash_attention_bf16_causal_8x32x4096x128"] = {"TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "frac_tensor_sustained": tf / pk["bf16_tflops_sustained"], "ms": t * 1e3}
     del Q, K_, V
     torch.cuda.empty_cache()
     return res
