@@ -404,3 +404,14 @@ def test_gemm_cta_pair_kernel(dt, M, N, K):
     check(y1, ref_f64.matmul(to_np(A), to_np(B)), "matmul", "pair MN")
     check(y2, ref_f64.matmul(to_np(A), to_np(W).T), "matmul", "pair K")
     check(y3, ref_f64.fused_mlp(to_np(A), to_np(wg), to_np(wu), to_np(wd)), "fused_mlp", "pair dual")
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 4096), (300, 1024), (8, 32768)])
+def test_layernorm_large_offset(rows, cols):
+    """Mean far from zero (1000 + N(0,1)): the merged per-thread variance stays accurate."""
+    r = _gen(51)
+    x = (1000.0 + r(rows, cols)).float()
+    w = torch.ones(cols)
+    b = torch.zeros(cols)
+    y = ops().layernorm(x.to(DEV), w.to(DEV), b.to(DEV))
+    check(y, ref_f64.layernorm(to_np(x), to_np(w), to_np(b)), "layernorm", "offset", scale_tol=100)
