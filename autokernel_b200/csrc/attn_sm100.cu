@@ -77,8 +77,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.x / p.H, h = blockIdx.x % p.H, hk = h / p.rep;
-  const int qblk = p.n_qblk - 1 - (int)blockIdx.y;  // heaviest (causal) blocks first
+  // Consecutive CTAs take the query blocks of one (batch, head), so the K/V blocks they
+  // all stream are shared in L2; heavy (late, causal) query blocks are dispatched first
+  // within each head.
+  const int bh = (int)blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H, hk = h / p.rep;
+  const int qblk = p.n_qblk - 1 - (int)blockIdx.x;
   const int q0 = qblk * 2 * BQ;
   // key blocks this CTA needs: all of them, or up to the diagonal of its last row
   int n_kv = (p.Sk + BKV - 1) / BKV;
@@ -348,7 +352,7 @@ static int launch(const AttnShape& a, cudaStream_t st) {
   });
   AK_REQUIRE(attr == cudaSuccess, AK_ERR_LAUNCH, "attention smem attribute: %s",
              cudaGetErrorString(attr));
-  dim3 grid((unsigned)(a.B * a.H), (unsigned)p.n_qblk);
+  dim3 grid((unsigned)p.n_qblk, (unsigned)(a.B * a.H));
   attn_kernel<DT, D><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tq, tk, tv, p);
   return launch_status("tc_attention");
 }
@@ -372,7 +376,8 @@ bool tc_attention_ok(const AttnShape& a) {
 
 int tc_attention(const AttnShape& a, cudaStream_t s) {
   AK_REQUIRE(a.B * a.H <= 0x7fffffffLL, AK_ERR_SHAPE, "batch*heads too large");
-  AK_REQUIRE((a.Sq + 255) / 256 <= 65535, AK_ERR_SHAPE, "sequence too long for the grid");
+  AK_REQUIRE(a.B * a.H <= 65535, AK_ERR_SHAPE, "batch*heads %lld exceeds 65535",
+             (long long)(a.B * a.H));
   if (a.dtype == AK_BF16) {
     if (a.D == 128) return attn::launch<AK_BF16, 128>(a, s);
     return attn::launch<AK_BF16, 64>(a, s);
