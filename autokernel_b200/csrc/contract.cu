@@ -12,10 +12,11 @@ namespace ak {
 bool tc_gemm_ok(int dtype, const void* A, const void* B, const void* B2, int64_t K, int64_t lda,
                 int64_t ldb, bool b_mn);
 int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, void* C, int M,
-            int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, cudaStream_t st);
+            int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R,
+            int64_t ldr, cudaStream_t st);
 int simt_gemm_any(int dtype, const void* A, const void* B, const void* B2, void* C, int M, int N,
                   int K, int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int act,
-                  cudaStream_t s);
+                  const void* R, int64_t ldr, cudaStream_t s);
 int simt_attention_any(int dtype, const void* Q, const void* K, const void* V, void* O,
                        int64_t bh, int Sq, int Sk, int D, int causal, float scale,
                        cudaStream_t s);
@@ -32,32 +33,39 @@ using namespace ak;
 
 extern "C" void ak_set_force_simt(int on) { g_force_simt = on; }
 
-extern "C" int ak_matmul(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
-                         int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int dtype,
-                         void* stream) {
+extern "C" int ak_matmul_add(const void* A, const void* B, void* C, const void* R, int64_t M,
+                             int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                             int64_t ldr, int b_kmajor, int dtype, void* stream) {
   AK_REQUIRE(dtype_ok(dtype), AK_ERR_DTYPE, "unsupported dtype %d", dtype);
   AK_REQUIRE(M >= 0 && N >= 0 && K >= 0, AK_ERR_SHAPE, "negative shape");
   AK_REQUIRE(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), AK_ERR_SHAPE,
              "dimension exceeds 2^31-1");
-  AK_REQUIRE(lda >= K && ldc >= N && ldb >= (b_kmajor ? K : N), AK_ERR_SHAPE,
-             "leading dimension too small");
+  AK_REQUIRE(lda >= K && ldc >= N && ldb >= (b_kmajor ? K : N) && (!R || ldr >= N),
+             AK_ERR_SHAPE, "leading dimension too small");
   if (M == 0 || N == 0) return AK_OK;
   AK_REQUIRE(A && B && C, AK_ERR_ARG, "null tensor pointer");
   cudaStream_t st = (cudaStream_t)stream;
   if (K == 0) {
-    // empty contraction: C = 0
-    cudaError_t e = cudaSuccess;
+    // empty contraction: C = R (or 0)
     const size_t es = dtype_size(dtype);
-    e = cudaMemset2DAsync(C, ldc * es, 0, N * es, M, st);
-    AK_REQUIRE(e == cudaSuccess, AK_ERR_LAUNCH, "memset: %s", cudaGetErrorString(e));
+    cudaError_t e = R ? cudaMemcpy2DAsync(C, ldc * es, R, ldr * es, N * es, M,
+                                          cudaMemcpyDeviceToDevice, st)
+                      : cudaMemset2DAsync(C, ldc * es, 0, N * es, M, st);
+    AK_REQUIRE(e == cudaSuccess, AK_ERR_LAUNCH, "empty contraction: %s", cudaGetErrorString(e));
     return AK_OK;
   }
   if (!g_force_simt && tc_gemm_ok(dtype, A, B, nullptr, K, lda, ldb, !b_kmajor) &&
       (b_kmajor || N % 8 == 0))
     return tc_gemm(dtype, b_kmajor ? 0 : 1, A, B, nullptr, C, (int)M, (int)N, (int)K, lda, ldb,
-                   ldc, 0, st);
+                   ldc, 0, R, ldr, st);
   return simt_gemm_any(dtype, A, B, nullptr, C, (int)M, (int)N, (int)K, lda, ldb, ldc, b_kmajor,
-                       0, st);
+                       0, R, ldr, st);
+}
+
+extern "C" int ak_matmul(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                         int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int dtype,
+                         void* stream) {
+  return ak_matmul_add(A, B, C, nullptr, M, N, K, lda, ldb, ldc, 0, b_kmajor, dtype, stream);
 }
 
 extern "C" int ak_mlp_gate_up(const void* x, const void* w_gate, const void* w_up, void* hidden,
@@ -74,9 +82,9 @@ extern "C" int ak_mlp_gate_up(const void* x, const void* w_gate, const void* w_u
   cudaStream_t st = (cudaStream_t)stream;
   if (!g_force_simt && D > 0 && tc_gemm_ok(dtype, x, w_gate, w_up, D, D, D, false))
     return tc_gemm(dtype, 2, x, w_gate, w_up, hidden, (int)M, (int)H, (int)D, D, D, H,
-                   activation, st);
+                   activation, nullptr, 0, st);
   return simt_gemm_any(dtype, x, w_gate, w_up, hidden, (int)M, (int)H, (int)D, D, D, H, 1,
-                       activation, st);
+                       activation, nullptr, 0, st);
 }
 
 extern "C" int ak_fused_mlp(const void* x, const void* w_gate, const void* w_up,

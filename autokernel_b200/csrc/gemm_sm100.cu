@@ -92,8 +92,10 @@ struct Params {
   int64_t ldc;
   int tiles_m, tiles_n, num_tiles;
   int act;
-  int vec_store;  // C rows are 16-byte aligned
+  int vec_store;  // C rows (and R rows) are 16-byte aligned
   uint32_t idesc;
+  const void* R;  // optional residual added in the epilogue (may alias C)
+  int64_t ldr;
 };
 
 AK_D void tile_coords(int t, const Params& p, int& tm, int& tn) {
@@ -112,17 +114,26 @@ AK_D void store_row32(const Params& p, int row, int col, const float* v) {
   using T = typename E::T;
   if (row >= p.M) return;
   T* c = reinterpret_cast<T*>(p.C) + (int64_t)row * p.ldc + col;
+  const T* rr = p.R ? reinterpret_cast<const T*>(p.R) + (int64_t)row * p.ldr + col : nullptr;
   if (p.vec_store && col + 32 <= p.N) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
+      float add[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (rr) {
+        const uint4 rv = reinterpret_cast<const uint4*>(rr)[q];
+        const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) add[j] = E::to_f(re[j]);
+      }
       uint4 raw;
       T* e = reinterpret_cast<T*>(&raw);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) e[j] = E::from_f(v[q * 8 + j]);
+      for (int j = 0; j < 8; ++j) e[j] = E::from_f(v[q * 8 + j] + add[j]);
       reinterpret_cast<uint4*>(c)[q] = raw;
     }
   } else {
-    for (int j = 0; j < 32 && col + j < p.N; ++j) c[j] = E::from_f(v[j]);
+    for (int j = 0; j < 32 && col + j < p.N; ++j)
+      c[j] = E::from_f(v[j] + (rr ? E::to_f(rr[j]) : 0.f));
   }
 }
 
@@ -492,7 +503,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 template <int DT, int MODE>
 static int launch(const void* A, const void* B, const void* B2, void* C, int M, int N, int K,
-                  int64_t lda, int64_t ldb, int64_t ldc, int act, cudaStream_t st) {
+                  int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R, int64_t ldr,
+                  cudaStream_t st) {
   CUtensorMap ta, tb, tb2;
   {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, str[1] = {(uint64_t)lda * 2};
@@ -526,7 +538,9 @@ static int launch(const void* A, const void* B, const void* B2, void* C, int M, 
   p.tiles_n = (N + bn_out - 1) / bn_out;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.act = act;
-  p.vec_store = (ldc % 8 == 0) && aligned16(C);
+  p.vec_store = (ldc % 8 == 0) && aligned16(C) && (!R || ((ldr % 8 == 0) && aligned16(R)));
+  p.R = R;
+  p.ldr = ldr;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, BM, BN, false, MODE == MODE_MN);
 
   static std::once_flag attr_once;
@@ -545,7 +559,8 @@ static int launch(const void* A, const void* B, const void* B2, void* C, int M, 
 
 template <int DT, int MODE>
 static int launch_pair(const void* A, const void* B, const void* B2, void* C, int M, int N,
-                       int K, int64_t lda, int64_t ldb, int64_t ldc, int act, cudaStream_t st) {
+                       int K, int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R,
+                       int64_t ldr, cudaStream_t st) {
   CUtensorMap ta, tb, tb2;
   {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, str[1] = {(uint64_t)lda * 2};
@@ -578,7 +593,9 @@ static int launch_pair(const void* A, const void* B, const void* B2, void* C, in
   p.tiles_n = (N + bn_out - 1) / bn_out;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.act = act;
-  p.vec_store = (ldc % 8 == 0) && aligned16(C);
+  p.vec_store = (ldc % 8 == 0) && aligned16(C) && (!R || ((ldr % 8 == 0) && aligned16(R)));
+  p.R = R;
+  p.ldr = ldr;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, 256, BN, false, MODE == MODE_MN);
 
   static std::once_flag attr_once;
@@ -622,7 +639,8 @@ bool tc_gemm_ok(int dtype, const void* A, const void* B, const void* B2, int64_t
 }
 
 int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, void* C, int M,
-            int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, cudaStream_t st) {
+            int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R,
+            int64_t ldr, cudaStream_t st) {
   using namespace gemm;
   // The CTA-pair kernel is opt-in (ak_set_gemm_pair / AK_GEMM_PAIR=1): measured at the
   // same throughput as the single-CTA kernel on the BASELINE shapes (both run at the
@@ -630,13 +648,13 @@ int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, v
   const bool pair = M > 128 && g_gemm_pair;
 #define AK_TCG(D)                                                                               \
   if (pair) {                                                                                   \
-    if (mode == MODE_K) return launch_pair<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, st); \
-    if (mode == MODE_MN) return launch_pair<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, st); \
-    return launch_pair<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, st);             \
+    if (mode == MODE_K) return launch_pair<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st); \
+    if (mode == MODE_MN) return launch_pair<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st); \
+    return launch_pair<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st);             \
   }                                                                                             \
-  if (mode == MODE_K) return launch<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, st);   \
-  if (mode == MODE_MN) return launch<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, st); \
-  return launch<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, st);
+  if (mode == MODE_K) return launch<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st);   \
+  if (mode == MODE_MN) return launch<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st); \
+  return launch<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st);
   if (dtype == AK_BF16) { AK_TCG(AK_BF16) }
   AK_TCG(AK_F16)
 #undef AK_TCG

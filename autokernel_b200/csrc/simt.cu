@@ -7,7 +7,7 @@
 //     which TMA cannot describe.
 // Accumulation is fp32 in a fixed order; no atomics (bitwise deterministic).
 //
-//   simt_gemm:  C = A @ op(B)      reference.py:10-12 (matmul_ref)
+//   simt_gemm:  C = A @ op(B) [+ R]  reference.py:10-12 (matmul_ref)
 //   simt_dual:  H = act(A @ Wg^T) * (A @ Wu^T)   first half of reference.py:45-55
 //   simt_attn:  O = softmax(Q K^T * scale [+ causal mask]) V   reference.py:32-42
 #include "ak_common.cuh"
@@ -23,7 +23,8 @@ template <int DT, bool DUAL>
 __global__ void __launch_bounds__(256) simt_gemm_kernel(const void* Av, const void* Bv,
                                                         const void* B2v, void* Cv, int M, int N,
                                                         int K, int64_t lda, int64_t ldb,
-                                                        int64_t ldc, int b_kmajor, int act) {
+                                                        int64_t ldc, int b_kmajor, int act,
+                                                        const void* Rv, int64_t ldr) {
   using E = Elem<DT>;
   using T = typename E::T;
   const T* A = reinterpret_cast<const T*>(Av);
@@ -86,6 +87,7 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const void* Av, const vo
       if (gn >= N) continue;
       float v = acc[i][j];
       if (DUAL) v = apply_act(act, v) * acc2[i][j];
+      if (Rv) v += E::to_f(reinterpret_cast<const T*>(Rv)[(int64_t)gm * ldr + gn]);
       C[(int64_t)gm * ldc + gn] = E::from_f(v);
     }
   }
@@ -152,21 +154,22 @@ __global__ void __launch_bounds__(128) simt_attn_kernel(const void* Qv, const vo
 
 template <int DT>
 int simt_gemm(const void* A, const void* B, const void* B2, void* C, int M, int N, int K,
-              int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int act, cudaStream_t s) {
+              int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int act, const void* R,
+              int64_t ldr, cudaStream_t s) {
   dim3 grid((N + SB_N - 1) / SB_N, (M + SB_M - 1) / SB_M);
   AK_REQUIRE(grid.y <= 65535u, AK_ERR_SHAPE, "M too large for the SIMT path");
-  if (B2) simt_gemm_kernel<DT, true><<<grid, 256, 0, s>>>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act);
-  else simt_gemm_kernel<DT, false><<<grid, 256, 0, s>>>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act);
+  if (B2) simt_gemm_kernel<DT, true><<<grid, 256, 0, s>>>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act, R, ldr);
+  else simt_gemm_kernel<DT, false><<<grid, 256, 0, s>>>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act, R, ldr);
   return launch_status("simt_gemm");
 }
 
 int simt_gemm_any(int dtype, const void* A, const void* B, const void* B2, void* C, int M, int N,
                   int K, int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int act,
-                  cudaStream_t s) {
+                  const void* R, int64_t ldr, cudaStream_t s) {
   switch (dtype) {
-    case AK_F32: return simt_gemm<AK_F32>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act, s);
-    case AK_F16: return simt_gemm<AK_F16>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act, s);
-    case AK_BF16: return simt_gemm<AK_BF16>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act, s);
+    case AK_F32: return simt_gemm<AK_F32>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act, R, ldr, s);
+    case AK_F16: return simt_gemm<AK_F16>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act, R, ldr, s);
+    case AK_BF16: return simt_gemm<AK_BF16>(A, B, B2, C, M, N, K, lda, ldb, ldc, b_kmajor, act, R, ldr, s);
   }
   set_error("unsupported dtype %d", dtype);
   return AK_ERR_DTYPE;

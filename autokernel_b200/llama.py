@@ -15,9 +15,10 @@ Every arithmetic step is one of this package's kernels:
     q/k/v/o projections  ops.linear            (tcgen05 GEMM, K-major weights, no copies)
     RoPE                 ops.rope_apply        (fp32 cos/sin table, [B, T, H, D] in place)
     attention            ops.attention_bhsd    (reads [B, T, H, D] views, GQA, causal)
-    SwiGLU MLP           ops.fused_mlp         (dual GEMM + SiLU*mul epilogue, down GEMM)
+    SwiGLU MLP           ops.mlp_hidden + ops.linear (dual GEMM + SiLU*mul epilogue, down GEMM)
+    residual adds        in the o-projection / down-projection GEMM epilogues, in place
     LM head + loss       ops.linear, ops.cross_entropy (ignore_index masks the last position)
-Glue left to torch: the embedding gather and the two residual adds per layer.
+Glue left to torch: the embedding gather.
 """
 from __future__ import annotations
 
@@ -134,10 +135,11 @@ class LlamaB200:
                                     k.transpose(1, 2).repeat_interleave(rep, 1),
                                     v.transpose(1, 2).repeat_interleave(rep, 1))
             o = o.transpose(1, 2).contiguous()
-        h = h + ops.linear(o.view(B, T, c.n_heads * hd), w[p + "attention.wo.weight"])
+        # residual adds happen in the GEMM epilogues, in place on h
+        ops.linear(o.view(B, T, c.n_heads * hd), w[p + "attention.wo.weight"], residual=h, out=h)
         x = ops.rmsnorm(h, w[p + "ffn_norm.weight"], c.norm_eps)
-        h = h + ops.fused_mlp(x, w[p + "feed_forward.w1.weight"], w[p + "feed_forward.w3.weight"],
-                              w[p + "feed_forward.w2.weight"])
+        hidden = ops.mlp_hidden(x, w[p + "feed_forward.w1.weight"], w[p + "feed_forward.w3.weight"])
+        ops.linear(hidden, w[p + "feed_forward.w2.weight"], residual=h, out=h)
         return h
 
     @torch.no_grad()
@@ -145,7 +147,7 @@ class LlamaB200:
         """Logits [B, T, vocab] (models/llama_7b.py:199-209)."""
         _, T = tokens.shape
         cos, sin = self._tables(T, tokens.device)
-        h = torch.nn.functional.embedding(tokens, self.w["tok_embeddings.weight"])
+        h = torch.nn.functional.embedding(tokens, self.w["tok_embeddings.weight"])  # new tensor
         for i in range(self.cfg.n_layers):
             h = self._layer(i, h, cos, sin)
         h = ops.rmsnorm(h, self.w["norm.weight"], self.cfg.norm_eps)

@@ -297,9 +297,47 @@ def matmul(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     return C.view(*A.shape[:-1], N)
 
 
-def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-    """x @ weight^T for an nn.Linear weight [N, K] (no copy of the weight)."""
-    return matmul(x, weight.t())
+def linear(x: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """x @ weight^T for an nn.Linear weight [N, K] (no copy of the weight).  With `residual`
+    (same shape as the result) the sum x @ weight^T + residual is formed in the GEMM epilogue;
+    `out` may be the residual itself for an in-place update."""
+    if residual is None and out is None:
+        return matmul(x, weight.t())
+    require_cuda(x, weight)
+    x2 = _rows_view(x).contiguous()
+    M, K = x2.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K or weight.dtype != x.dtype:
+        raise ValueError("linear: weight must be [N, K] of x's dtype")
+    w = weight.contiguous()
+    shape = (*x.shape[:-1], N)
+    o = torch.empty(shape, dtype=x.dtype, device=x.device) if out is None else out
+    if tuple(o.shape) != shape or not o.is_contiguous():
+        raise ValueError("linear: out must be a contiguous tensor of the result shape")
+    r = None
+    if residual is not None:
+        if tuple(residual.shape) != shape or residual.dtype != x.dtype:
+            raise ValueError("linear: residual must match the result shape and dtype")
+        r = residual if residual.is_contiguous() else residual.contiguous()
+    call("ak_matmul_add", x2.data_ptr(), w.data_ptr(), o.data_ptr(),
+         r.data_ptr() if r is not None else None, M, N, K, x2.stride(0), K, N, N, 1,
+         dtype_code(x.dtype), stream_ptr(x.device))
+    return o
+
+
+def mlp_hidden(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+               activation: str = "silu") -> torch.Tensor:
+    """act(x @ w_gate^T) * (x @ w_up^T) from one dual-B tensor-core GEMM."""
+    require_cuda(x, w_gate, w_up)
+    x2 = _rows_view(x).contiguous()
+    M, D = x2.shape
+    H = w_gate.shape[0]
+    hidden = torch.empty((*x.shape[:-1], H), dtype=x.dtype, device=x.device)
+    call("ak_mlp_gate_up", x2.data_ptr(), w_gate.contiguous().data_ptr(),
+         w_up.contiguous().data_ptr(), hidden.data_ptr(), M, D, H, _lib.AK_ACT[activation],
+         dtype_code(x.dtype), stream_ptr(x.device))
+    return hidden
 
 
 def fused_mlp(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,

@@ -154,6 +154,15 @@ AK_API int ak_mean_from_sum_count(const double* sum_count, void* out, int out_dt
 AK_API int ak_matmul(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
               int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int dtype, void* stream);
 
+/* C[M, N] = A @ B + R: ak_matmul with a residual [M, N] (leading dimension ldr) added in the
+ * epilogue before rounding; R may alias C (in-place residual update, each element read then
+ * written by the same thread).  Fuses the residual adds around the o-projection and the MLP
+ * down projection of models/llama_7b.py:110-111 into the GEMM (fused neighbour of the path;
+ * matmul semantics of reference.py:10-12). */
+AK_API int ak_matmul_add(const void* A, const void* B, void* C, const void* R, int64_t M,
+                         int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                         int64_t ldr, int b_kmajor, int dtype, void* stream);
+
 /* hidden[M, H] = act(x @ w_gate^T) * (x @ w_up^T) for contiguous x [M, D],
  * w_gate / w_up [H, D].  First stage of kernels/fused_mlp.py:102. */
 AK_API int ak_mlp_gate_up(const void* x, const void* w_gate, const void* w_up, void* hidden, int64_t M,

@@ -415,3 +415,19 @@ def test_layernorm_large_offset(rows, cols):
     b = torch.zeros(cols)
     y = ops().layernorm(x.to(DEV), w.to(DEV), b.to(DEV))
     check(y, ref_f64.layernorm(to_np(x), to_np(w), to_np(b)), "layernorm", "offset", scale_tol=100)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("M,N,K,inplace", [(300, 256, 512, False), (256, 520, 136, True),
+                                           (1023, 1023, 1023, True)])
+def test_linear_with_residual(dt, M, N, K, inplace):
+    """C = x @ W^T + R formed in the GEMM epilogue; R may be C itself."""
+    r = _gen(M + K)
+    x = r(M, K, scale=1 / math.sqrt(K)).to(DTS[dt])
+    W = r(N, K).to(DTS[dt])
+    R = r(M, N).to(DTS[dt])
+    Rd = R.to(DEV)
+    y = ops().linear(x.to(DEV), W.to(DEV), residual=Rd, out=Rd if inplace else None)
+    if inplace:
+        assert y.data_ptr() == Rd.data_ptr()
+    check(y, ref_f64.matmul(to_np(x), to_np(W).T) + to_np(R), "matmul", "residual")
