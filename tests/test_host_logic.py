@@ -59,3 +59,34 @@ def test_cpu_tensors_are_rejected(name):
     }[name]
     with pytest.raises(ValueError, match="CUDA"):
         ops.OPS[name](*args)
+
+
+# kernel_fn signatures of the reference starters (kernels/<op>.py), which AutoKernel's bench.py
+# calls with keyword arguments named after its input generators (bench.py:203-276)
+REFERENCE_SIGNATURES = {
+    "matmul": [("A", None), ("B", None)],
+    "softmax": [("x", None)],
+    "layernorm": [("x", None), ("weight", None), ("bias", None), ("eps", 1e-5)],
+    "rmsnorm": [("x", None), ("weight", None), ("eps", 1e-6)],
+    "flash_attention": [("Q", None), ("K", None), ("V", None), ("causal", True), ("sm_scale", None)],
+    "fused_mlp": [("x", None), ("w_gate", None), ("w_up", None), ("w_down", None),
+                  ("activation", "silu")],
+    "cross_entropy": [("logits", None), ("targets", None)],
+    "rotary_embedding": [("x", None), ("cos", None), ("sin", None)],
+    "reduce": [("x", None), ("dim", -1)],
+}
+
+
+@pytest.mark.parametrize("name", list(REFERENCE_SIGNATURES))
+def test_drop_in_kernel_fn_signature(name):
+    import inspect
+
+    from autokernel_b200 import kernels
+    mod = kernels.get(name)
+    assert mod.KERNEL_TYPE == name
+    params = list(inspect.signature(mod.kernel_fn).parameters.values())
+    got = [(p.name, None if p.default is inspect.Parameter.empty else p.default) for p in params]
+    assert got == REFERENCE_SIGNATURES[name]
+    # the ops-level function takes the same arguments
+    op_params = list(inspect.signature(ops.OPS[name]).parameters)
+    assert op_params == [n for n, _ in REFERENCE_SIGNATURES[name]]
