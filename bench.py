@@ -499,13 +499,13 @@ def reference_arm(args):
     for _ in range(args.warmup):
         _cpu_step(d)
     t0 = time.perf_counter()
-    for _ in range(args.ref_steps):
+    for _ in range(args.steps):
         _cpu_step(d)
-    dt = (time.perf_counter() - t0) / args.ref_steps
+    dt = (time.perf_counter() - t0) / args.steps
     value = nbytes / dt / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.ref_steps, "warmup": args.warmup,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16 (reduce: fp32)", "data": "synthetic (seeded)",
         "config": {"workload": "configs[1] memory-bound sweep, bounded CPU sample (rank 0 only)"},
@@ -525,7 +525,6 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--op-reps", type=int, default=20)
-    ap.add_argument("--ref-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-ops", action="store_true", help="skip the GEMM/MLP/attention/CE/RMSNorm lines")
     ap.add_argument("--no-e2e", action="store_true")
