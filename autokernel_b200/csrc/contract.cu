@@ -5,15 +5,11 @@
 // call is bitwise reproducible.
 #include "ak_common.cuh"
 #include "attn.cuh"
+#include "gemm.cuh"
 
 #include <cstdlib>
 
 namespace ak {
-bool tc_gemm_ok(int dtype, const void* A, const void* B, const void* B2, int64_t K, int64_t lda,
-                int64_t ldb, bool b_mn);
-int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, void* C, int M,
-            int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R,
-            int64_t ldr, cudaStream_t st);
 int simt_gemm_any(int dtype, const void* A, const void* B, const void* B2, void* C, int M, int N,
                   int K, int64_t lda, int64_t ldb, int64_t ldc, int b_kmajor, int act,
                   const void* R, int64_t ldr, cudaStream_t s);
@@ -57,9 +53,36 @@ extern "C" int ak_matmul_add(const void* A, const void* B, void* C, const void* 
   if (!g_force_simt && tc_gemm_ok(dtype, A, B, nullptr, K, lda, ldb, !b_kmajor) &&
       (b_kmajor || N % 8 == 0))
     return tc_gemm(dtype, b_kmajor ? 0 : 1, A, B, nullptr, C, (int)M, (int)N, (int)K, lda, ldb,
-                   ldc, 0, R, ldr, st);
+                   ldc, 0, R, ldr, RopeEpilogue(), st);
   return simt_gemm_any(dtype, A, B, nullptr, C, (int)M, (int)N, (int)K, lda, ldb, ldc, b_kmajor,
                        0, R, ldr, st);
+}
+
+extern "C" int ak_linear_rope(const void* x, const void* w, void* out, int64_t M, int64_t N,
+                              int64_t K, int64_t ldx, int64_t ldo, const float* cos,
+                              const float* sin, int64_t T, int64_t head_dim, int64_t rope_cols,
+                              int dtype, void* stream) {
+  AK_REQUIRE(dtype == AK_F16 || dtype == AK_BF16, AK_ERR_DTYPE,
+             "ak_linear_rope: 16-bit inputs only (tensor-core epilogue)");
+  AK_REQUIRE(M >= 0 && N > 0 && K > 0 && M < (1LL << 31) && N < (1LL << 31) &&
+                 K < (1LL << 31),
+             AK_ERR_SHAPE, "bad shape");
+  AK_REQUIRE(ldx >= K && ldo >= N, AK_ERR_SHAPE, "leading dimension too small");
+  AK_REQUIRE(T > 0 && T < (1LL << 31) && head_dim % 32 == 0 && head_dim > 0 &&
+                 rope_cols >= 0 && rope_cols <= N && rope_cols % head_dim == 0,
+             AK_ERR_SHAPE, "rope: need head_dim a multiple of 32 and rope_cols a multiple of it");
+  if (M == 0) return AK_OK;
+  AK_REQUIRE(x && w && out && (rope_cols == 0 || (cos && sin)), AK_ERR_ARG, "null pointer");
+  AK_REQUIRE(!g_force_simt && tc_gemm_ok(dtype, x, w, nullptr, K, ldx, K, false),
+             AK_ERR_UNSUPPORTED, "ak_linear_rope needs TMA-describable operands on sm_100");
+  RopeEpilogue rope;
+  rope.cos = cos;
+  rope.sin = sin;
+  rope.T = (int)T;
+  rope.head_dim = (int)head_dim;
+  rope.cols = (int)rope_cols;
+  return tc_gemm(dtype, 0, x, w, nullptr, out, (int)M, (int)N, (int)K, ldx, K, ldo, 0, nullptr,
+                 0, rope, (cudaStream_t)stream);
 }
 
 extern "C" int ak_matmul(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
@@ -82,7 +105,7 @@ extern "C" int ak_mlp_gate_up(const void* x, const void* w_gate, const void* w_u
   cudaStream_t st = (cudaStream_t)stream;
   if (!g_force_simt && D > 0 && tc_gemm_ok(dtype, x, w_gate, w_up, D, D, D, false))
     return tc_gemm(dtype, 2, x, w_gate, w_up, hidden, (int)M, (int)H, (int)D, D, D, H,
-                   activation, nullptr, 0, st);
+                   activation, nullptr, 0, RopeEpilogue(), st);
   return simt_gemm_any(dtype, x, w_gate, w_up, hidden, (int)M, (int)H, (int)D, D, D, H, 1,
                        activation, nullptr, 0, st);
 }

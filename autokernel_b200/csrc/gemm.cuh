@@ -1,0 +1,21 @@
+// Host-side interface of the tcgen05 GEMM (gemm_sm100.cu) used by the C ABI.
+#pragma once
+#include "ak_common.cuh"
+
+namespace ak {
+
+// Rotary embedding applied in the GEMM epilogue to output columns [0, cols): interleaved
+// pairs inside head_dim-wide column groups, position = row % T, fp32 cos/sin [T, head_dim / 2].
+struct RopeEpilogue {
+  const float* cos = nullptr;
+  const float* sin = nullptr;
+  int T = 1, head_dim = 2, cols = 0;
+};
+
+bool tc_gemm_ok(int dtype, const void* A, const void* B, const void* B2, int64_t K, int64_t lda,
+                int64_t ldb, bool b_mn);
+int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, void* C, int M,
+            int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R,
+            int64_t ldr, const RopeEpilogue& rope, cudaStream_t st);
+
+}  // namespace ak

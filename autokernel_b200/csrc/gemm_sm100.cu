@@ -20,6 +20,7 @@
 // Every mbarrier wait is bounded (see sm100.cuh).
 #include "sm100.cuh"
 #include "ak_act.cuh"
+#include "gemm.cuh"
 
 #include <cudaTypedefs.h>
 #include <cstdlib>
@@ -96,6 +97,11 @@ struct Params {
   uint32_t idesc;
   const void* R;  // optional residual added in the epilogue (may alias C)
   int64_t ldr;
+  // optional rotary embedding of output columns [0, rope_cols): interleaved pairs within
+  // head_dim-wide groups, position = row % rope_T, fp32 tables [rope_T, rope_hd / 2]
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_T, rope_hd, rope_cols;
 };
 
 AK_D void tile_coords(int t, const Params& p, int& tm, int& tn) {
@@ -106,6 +112,26 @@ AK_D void tile_coords(int t, const Params& p, int& tm, int& tn) {
   const int r = t - g * group;
   tm = first + r % gsz;
   tn = r / gsz;
+}
+
+// Rotate the (even, odd) column pairs of 32 consecutive outputs of one row
+// (reference.py:63-69 applied to the projection output, before rounding).
+AK_D void rope_row32(const Params& p, int row, int col, float* v) {
+  if (!p.rope_cos || col >= p.rope_cols || row >= p.M) return;
+  const int t = row % p.rope_T;
+  const int half = p.rope_hd >> 1;
+  const float* cs = p.rope_cos + (int64_t)t * half;
+  const float* sn = p.rope_sin + (int64_t)t * half;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int c = col + 2 * j;
+    if (c >= p.rope_cols) break;
+    const int i = (c % p.rope_hd) >> 1;
+    const float co = __ldg(cs + i), si = __ldg(sn + i);
+    const float x1 = v[2 * j], x2 = v[2 * j + 1];
+    v[2 * j] = fmaf(x1, co, -x2 * si);
+    v[2 * j + 1] = fmaf(x1, si, x2 * co);
+  }
 }
 
 template <int DT>
@@ -274,6 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          rope_row32(p, row, tn * BN + c, v);
           store_row32<DT>(p, row, tn * BN + c, v);
         }
       } else {
@@ -471,6 +498,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          rope_row32(p, row, tn * BN + c, v);
           store_row32<DT>(p, row, tn * BN + c, v);
         }
       } else {
@@ -504,7 +532,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 template <int DT, int MODE>
 static int launch(const void* A, const void* B, const void* B2, void* C, int M, int N, int K,
                   int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R, int64_t ldr,
-                  cudaStream_t st) {
+                  const RopeEpilogue& rope, cudaStream_t st) {
   CUtensorMap ta, tb, tb2;
   {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, str[1] = {(uint64_t)lda * 2};
@@ -541,6 +569,11 @@ static int launch(const void* A, const void* B, const void* B2, void* C, int M, 
   p.vec_store = (ldc % 8 == 0) && aligned16(C) && (!R || ((ldr % 8 == 0) && aligned16(R)));
   p.R = R;
   p.ldr = ldr;
+  p.rope_cos = rope.cos;
+  p.rope_sin = rope.sin;
+  p.rope_T = rope.T;
+  p.rope_hd = rope.head_dim;
+  p.rope_cols = rope.cols;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, BM, BN, false, MODE == MODE_MN);
 
   static std::once_flag attr_once;
@@ -560,7 +593,7 @@ static int launch(const void* A, const void* B, const void* B2, void* C, int M, 
 template <int DT, int MODE>
 static int launch_pair(const void* A, const void* B, const void* B2, void* C, int M, int N,
                        int K, int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R,
-                       int64_t ldr, cudaStream_t st) {
+                       int64_t ldr, const RopeEpilogue& rope, cudaStream_t st) {
   CUtensorMap ta, tb, tb2;
   {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, str[1] = {(uint64_t)lda * 2};
@@ -596,6 +629,11 @@ static int launch_pair(const void* A, const void* B, const void* B2, void* C, in
   p.vec_store = (ldc % 8 == 0) && aligned16(C) && (!R || ((ldr % 8 == 0) && aligned16(R)));
   p.R = R;
   p.ldr = ldr;
+  p.rope_cos = rope.cos;
+  p.rope_sin = rope.sin;
+  p.rope_T = rope.T;
+  p.rope_hd = rope.head_dim;
+  p.rope_cols = rope.cols;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, 256, BN, false, MODE == MODE_MN);
 
   static std::once_flag attr_once;
@@ -640,7 +678,7 @@ bool tc_gemm_ok(int dtype, const void* A, const void* B, const void* B2, int64_t
 
 int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, void* C, int M,
             int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R,
-            int64_t ldr, cudaStream_t st) {
+            int64_t ldr, const RopeEpilogue& rope, cudaStream_t st) {
   using namespace gemm;
   // The CTA-pair kernel is opt-in (ak_set_gemm_pair / AK_GEMM_PAIR=1): measured at the
   // same throughput as the single-CTA kernel on the BASELINE shapes (both run at the
@@ -648,13 +686,13 @@ int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, v
   const bool pair = M > 128 && g_gemm_pair;
 #define AK_TCG(D)                                                                               \
   if (pair) {                                                                                   \
-    if (mode == MODE_K) return launch_pair<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st); \
-    if (mode == MODE_MN) return launch_pair<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st); \
-    return launch_pair<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st);             \
+    if (mode == MODE_K) return launch_pair<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st); \
+    if (mode == MODE_MN) return launch_pair<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st); \
+    return launch_pair<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st);             \
   }                                                                                             \
-  if (mode == MODE_K) return launch<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st);   \
-  if (mode == MODE_MN) return launch<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st); \
-  return launch<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, st);
+  if (mode == MODE_K) return launch<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st);   \
+  if (mode == MODE_MN) return launch<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st); \
+  return launch<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st);
   if (dtype == AK_BF16) { AK_TCG(AK_BF16) }
   AK_TCG(AK_F16)
 #undef AK_TCG

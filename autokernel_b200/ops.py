@@ -326,6 +326,26 @@ def linear(x: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor | None 
     return o
 
 
+def linear_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                seq_len: int, head_dim: int, rope_cols: int) -> torch.Tensor:
+    """x @ weight^T with interleaved RoPE applied in the GEMM epilogue to the first rope_cols
+    output columns (head_dim-wide groups); row r of the flattened x is position r % seq_len.
+    cos / sin: fp32 [seq_len, head_dim / 2] (any broadcastable view that is contiguous)."""
+    require_cuda(x, weight, cos, sin)
+    x2 = _rows_view(x).contiguous()
+    M, K = x2.shape
+    N = weight.shape[0]
+    c = cos.reshape(-1, head_dim // 2).float().contiguous()
+    s_ = sin.reshape(-1, head_dim // 2).float().contiguous()
+    if c.shape[0] != seq_len:
+        raise ValueError("cos/sin must hold seq_len rows")
+    out = torch.empty((*x.shape[:-1], N), dtype=x.dtype, device=x.device)
+    call("ak_linear_rope", x2.data_ptr(), weight.contiguous().data_ptr(), out.data_ptr(), M, N, K,
+         x2.stride(0), N, c.data_ptr(), s_.data_ptr(), seq_len, head_dim, rope_cols,
+         dtype_code(x.dtype), stream_ptr(x.device))
+    return out
+
+
 def mlp_hidden(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
                activation: str = "silu") -> torch.Tensor:
     """act(x @ w_gate^T) * (x @ w_up^T) from one dual-B tensor-core GEMM."""

@@ -163,6 +163,16 @@ AK_API int ak_matmul_add(const void* A, const void* B, void* C, const void* R, i
                          int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
                          int64_t ldr, int b_kmajor, int dtype, void* stream);
 
+/* out[M, N] = x[M, K] @ w[N, K]^T with rotary embedding applied in the GEMM epilogue to
+ * output columns [0, rope_cols): interleaved (even, odd) pairs within head_dim-wide column
+ * groups, position = row % T, fp32 cos/sin [T, head_dim / 2].  Fuses the fused q/k/v
+ * projection with apply_rotary_emb (models/llama_7b.py:40-48, 67-71; RoPE math of
+ * reference.py:63-69).  16-bit inputs, tensor-core path only (AK_ERR_UNSUPPORTED otherwise). */
+AK_API int ak_linear_rope(const void* x, const void* w, void* out, int64_t M, int64_t N,
+                          int64_t K, int64_t ldx, int64_t ldo, const float* cos,
+                          const float* sin, int64_t T, int64_t head_dim, int64_t rope_cols,
+                          int dtype, void* stream);
+
 /* hidden[M, H] = act(x @ w_gate^T) * (x @ w_up^T) for contiguous x [M, D],
  * w_gate / w_up [H, D].  First stage of kernels/fused_mlp.py:102. */
 AK_API int ak_mlp_gate_up(const void* x, const void* w_gate, const void* w_up, void* hidden, int64_t M,

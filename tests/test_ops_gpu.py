@@ -431,3 +431,20 @@ def test_linear_with_residual(dt, M, N, K, inplace):
     if inplace:
         assert y.data_ptr() == Rd.data_ptr()
     check(y, ref_f64.matmul(to_np(x), to_np(W).T) + to_np(R), "matmul", "residual")
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("B,T,H,Hkv,hd", [(2, 100, 4, 2, 64), (1, 300, 2, 2, 128)])
+def test_linear_rope_epilogue(dt, B, T, H, Hkv, hd):
+    """Fused q/k/v projection: RoPE on the q and k columns at position row % T, v untouched."""
+    r = _gen(T + hd)
+    D = 256
+    x = r(B, T, D).to(DTS[dt])
+    W = r((H + 2 * Hkv) * hd, D, scale=0.05).to(DTS[dt])
+    c, s = ref_f64.cos_sin_table(T, hd // 2)
+    ct, st = torch.tensor(c, dtype=torch.float32), torch.tensor(s, dtype=torch.float32)
+    y = ops().linear_rope(x.to(DEV), W.to(DEV), ct.to(DEV), st.to(DEV), T, hd, (H + Hkv) * hd)
+    proj = (to_np(x) @ to_np(W).T).reshape(B, T, H + 2 * Hkv, hd)
+    e = proj.copy()
+    e[:, :, :H + Hkv] = ref_f64.rotary_embedding(proj[:, :, :H + Hkv], c[:, None, :], s[:, None, :])
+    check(y, e.reshape(B, T, -1), "matmul", "linear_rope")
