@@ -19,8 +19,6 @@
 #include "ak_common.cuh"
 #include "rowring.cuh"
 
-#include <cstdlib>
-
 namespace ak {
 
 enum RowOp { OP_RMS = 0, OP_LN = 1, OP_SOFTMAX = 2 };
@@ -242,12 +240,8 @@ static int run_rowop(const RowArgs& a, cudaStream_t s) {
   if (vec_ok && nv <= 1024 * 8) {
     // Aim for 4 vectors per thread (enough loads in flight per thread),
     // then round the per-thread count up to a supported template value.
-    static const int target = [] {
-      const char* e = getenv("AK_ROW_VPT");
-      return e ? atoi(e) : 4;
-    }();
     int64_t g = 32;
-    while (g < 1024 && g * target < nv) g <<= 1;
+    while (g < 1024 && g * 4 < nv) g <<= 1;
     int64_t vpt = (nv + g - 1) / g;
     int V = vpt <= 1 ? 1 : vpt <= 2 ? 2 : vpt <= 4 ? 4 : 8;
     switch (V) {

@@ -448,3 +448,25 @@ def test_linear_rope_epilogue(dt, B, T, H, Hkv, hd):
     e = proj.copy()
     e[:, :, :H + Hkv] = ref_f64.rotary_embedding(proj[:, :, :H + Hkv], c[:, None, :], s[:, None, :])
     check(y, e.reshape(B, T, -1), "matmul", "linear_rope")
+
+
+@pytest.mark.parametrize("op", OPS)
+def test_cuda_graph_capture(op):
+    """Every operator can be captured in a CUDA graph (no host synchronisation or device
+    allocation inside the C ABI) and replays to the eager result."""
+    case = load_golden(op)[0]
+    ins = {k: v.to(DEV) for k, v in case["inputs"].items()}
+    kw = case["kwargs"]
+    eager = _run(op, {k: v for k, v in ins.items()}, kw)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        _run(op, ins, kw)  # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = _run(op, ins, kw)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
