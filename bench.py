@@ -327,9 +327,6 @@ def ours(args):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        # rank 0's stdout must carry only the JSON line; NCCL's version banner goes away
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", device_id=device)
     pk = peaks()
     d = W.sweep_inputs(device, seed=rank, scale=args.scale)
@@ -411,7 +408,7 @@ def ours(args):
     if cpu:
         line["cpu_baseline"] = cpu
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
 
@@ -514,10 +511,30 @@ def reference_arm(args):
                                    "reduce 2^27 fp32 per step (reference.py ops on CPU tensors)"},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Write the result line to the process's original stdout."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
+def _reserve_stdout() -> None:
+    """Keep the original stdout for the JSON line only: anything else written to file
+    descriptor 1 (NCCL's banner, library messages) goes to stderr."""
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
 
 
 def main(argv=None):
+    _reserve_stdout()
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
