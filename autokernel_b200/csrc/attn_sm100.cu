@@ -29,6 +29,7 @@
 // its TMEM and records AK_STATUS_TIMEOUT in the device status word.
 #include "sm100.cuh"
 
+#include <cstdlib>
 #include <mutex>
 
 #include "attn.cuh"
@@ -214,6 +215,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r + c * 32);
       tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_regs_ready(r + c * 32);
       // no per-element masks when every row of the warp sees the whole block
       const bool full = __all_sync(0xffffffffu, kmax >= BKV);
       if (!full) {
@@ -240,6 +243,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t o[32];
           tmem_ld32(t_o + c * 32, o);
           tmem_wait_ld();
+          tmem_regs_ready(o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
           tmem_st32(t_o + c * 32, o);
@@ -287,6 +291,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t r[32];
         tmem_ld32(t_o + c * 32, r);
         tmem_wait_ld();
+        tmem_regs_ready(r);
         if (qrow < p.Sq) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -374,10 +379,19 @@ bool tc_attention_ok(const AttnShape& a) {
   return device_info().cc_major == 10;
 }
 
+// The CTA-pair kernel is opt-in (ak_set_attn_pair / AK_ATTN_PAIR=1): it is correct and
+// pipelines Q K^T ahead of the softmax, but both kernels are bound by the softmax's
+// exponential throughput and the single-CTA one measured faster.
+int g_attn_pair = [] {
+  const char* e = getenv("AK_ATTN_PAIR");
+  return (e && e[0] == '1') ? 1 : 0;
+}();
+
 int tc_attention(const AttnShape& a, cudaStream_t s) {
   AK_REQUIRE(a.B * a.H <= 0x7fffffffLL, AK_ERR_SHAPE, "batch*heads too large");
   AK_REQUIRE(a.B * a.H <= 65535, AK_ERR_SHAPE, "batch*heads %lld exceeds 65535",
              (long long)(a.B * a.H));
+  if (a.D == 128 && g_attn_pair) return tc_attention_pair(a, s);
   if (a.dtype == AK_BF16) {
     if (a.D == 128) return attn::launch<AK_BF16, 128>(a, s);
     return attn::launch<AK_BF16, 64>(a, s);
@@ -387,3 +401,5 @@ int tc_attention(const AttnShape& a, cudaStream_t s) {
 }
 
 }  // namespace ak
+
+extern "C" void ak_set_attn_pair(int on) { ak::g_attn_pair = on ? 1 : 0; }

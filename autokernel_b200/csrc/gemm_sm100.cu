@@ -297,6 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t r[32];
           tmem_ld32(tbase + c, r);
           tmem_wait_ld();
+          tmem_regs_ready(r);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -310,6 +311,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld32(tbase + c, g);
           tmem_ld32(tbase + BN / 2 + c, u);
           tmem_wait_ld();
+          tmem_regs_ready(g);
+          tmem_regs_ready(u);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j)
@@ -495,6 +498,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t r[32];
           tmem_ld32(tbase + c, r);
           tmem_wait_ld();
+          tmem_regs_ready(r);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -508,6 +512,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld32(tbase + c, g);
           tmem_ld32(tbase + BN / 2 + c, u);
           tmem_wait_ld();
+          tmem_regs_ready(g);
+          tmem_regs_ready(u);
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j)

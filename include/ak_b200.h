@@ -64,6 +64,10 @@ AK_API void ak_set_force_simt(int on);
  * kernel instead of the single-CTA one (also AK_GEMM_PAIR=1 at load time).  Same results
  * within rounding order of the accumulator; no reference counterpart (a kernel choice). */
 AK_API void ak_set_gemm_pair(int on);
+/* 1 runs head_dim-128 attention on the CTA-pair (cta_group::2) tcgen05 kernel instead of
+ * the single-CTA one (also AK_ATTN_PAIR=1 at load time).  Same results within rounding of
+ * the exponentials; no reference counterpart (a kernel choice). */
+AK_API void ak_set_attn_pair(int on);
 
 /* ----------------------------------------------------------------- row ops */
 

@@ -363,10 +363,12 @@ def test_flash_attention_noncontiguous_inputs():
 
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
 @pytest.mark.parametrize("case", ["q_is_k", "rising_keys"])
-def test_attention_row_max_jumps(dt, case):
+@pytest.mark.parametrize("pair", [0, 1])
+def test_attention_row_max_jumps(dt, case, pair):
     """Rows whose running max grows by a lot in a later key block (self-similar queries and
     keys put the largest score on the diagonal; growing key norms push it to the last block).
-    This exercises the rescale of the TMEM accumulator for some rows of a warp and not others."""
+    This exercises the rescale of the TMEM accumulator for some rows of a warp and not others,
+    on both tensor-core kernels."""
     r = _gen(41)
     B, H, S, D = 2, 4, 640, 128
     q = r(B, H, S, D)
@@ -376,10 +378,52 @@ def test_attention_row_max_jumps(dt, case):
         k = r(B, H, S, D) * torch.linspace(0.2, 3.0, S)[None, None, :, None]
     v = r(B, H, S, D)
     q, k, v = (t.to(DTS[dt]) for t in (q, k, v))
-    y = ops().flash_attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=True)
-    check(y, ref_f64.attention(to_np(q), to_np(k), to_np(v), True), "flash_attention", case)
     from autokernel_b200 import _lib
+    _lib.load().ak_set_attn_pair(pair)
+    try:
+        for causal in (True, False):
+            y = ops().flash_attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+            check(y, ref_f64.attention(to_np(q), to_np(k), to_np(v), causal), "flash_attention",
+                  f"{case} causal={causal}")
+    finally:
+        _lib.load().ak_set_attn_pair(0)
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("B,H,S,causal", [(1, 2, 2048, True), (1, 2, 1536, False),
+                                          (2, 2, 700, True), (1, 3, 1100, False)])
+@pytest.mark.parametrize("pair", [1, 0])
+def test_attention_d128_both_kernels(dt, B, H, S, causal, pair):
+    """head_dim 128 runs on the single-CTA kernel (default) or the CTA-pair one; long rows
+    reach the mask-free blocks whose exponentials partly run on the FMA pipe, ragged S
+    leaves the second 256-row tile of a pair partly or wholly past the end."""
+    from autokernel_b200 import _lib
+    r = _gen(S + 7 * H)
+    Q, K, V = (r(B, H, S, 128).to(DTS[dt]) for _ in range(3))
+    _lib.load().ak_set_attn_pair(pair)
+    try:
+        y = ops().flash_attention(Q.to(DEV), K.to(DEV), V.to(DEV), causal=causal)
+        torch.cuda.synchronize()
+    finally:
+        _lib.load().ak_set_attn_pair(0)
+    check(y, ref_f64.attention(to_np(Q), to_np(K), to_np(V), causal), "flash_attention",
+          f"pair={pair} {B}x{H}x{S}")
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_attention_pair_wide_scores(dt):
+    """Scores spread over a wide range (scaled keys): exponent arguments far below -125
+    exercise the clamp of the FMA-pipe exponential."""
+    r = _gen(77)
+    B, H, S, D = 1, 2, 1024, 128
+    q = r(B, H, S, D)
+    k = r(B, H, S, D) * torch.linspace(0.5, 12.0, S)[None, None, :, None]
+    v = r(B, H, S, D)
+    q, k, v = (t.to(DTS[dt]) for t in (q, k, v))
+    y = ops().flash_attention(q.to(DEV), k.to(DEV), v.to(DEV), causal=False)
+    check(y, ref_f64.attention(to_np(q), to_np(k), to_np(v), False), "flash_attention", "wide")
 
 
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
