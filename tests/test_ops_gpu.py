@@ -450,7 +450,7 @@ def test_gemm_cta_pair_kernel(dt, M, N, K):
     check(y3, ref_f64.fused_mlp(to_np(A), to_np(wg), to_np(wu), to_np(wd)), "fused_mlp", "pair dual")
 
 
-@pytest.mark.parametrize("rows,cols", [(64, 4096), (300, 1024), (8, 32768)])
+@pytest.mark.parametrize("rows,cols", [(64, 4096), (300, 1024), (8, 32768), (8000, 4096)])
 def test_layernorm_large_offset(rows, cols):
     """Mean far from zero (1000 + N(0,1)): the merged per-thread variance stays accurate."""
     r = _gen(51)
