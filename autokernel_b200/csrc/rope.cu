@@ -14,6 +14,8 @@
 // fp32 with a single rounding at the store.
 #include "ak_common.cuh"
 
+#include <type_traits>
+
 namespace ak {
 
 struct RopeArgs {
@@ -40,6 +42,17 @@ AK_D void load_cs(const typename Elem<CDT>::T* p, float* out) {
     for (int i = 0; i < N; ++i) out[i] = Elem<CDT>::to_f(e[i]);
   }
 }
+
+// cos/sin pieces kept as the raw loaded words until the arithmetic (half the registers of
+// the widened floats for 16-bit tables), so more vectors stay in flight per SM.
+template <int CDT, int N>
+struct CsRaw {
+  using T = typename Elem<CDT>::T;
+  using W = typename std::conditional<sizeof(T) * N == 8, uint2, uint4>::type;
+  W w;
+  AK_D void load(const T* p) { w = __ldg(reinterpret_cast<const W*>(p)); }
+  AK_D float at(int i) const { return Elem<CDT>::to_f(reinterpret_cast<const T*>(&w)[i]); }
+};
 
 template <int DT, int CDT>
 __global__ void __launch_bounds__(256) rope_vec_kernel(RopeArgs a) {
@@ -105,7 +118,7 @@ __global__ void __launch_bounds__(256) rope_vec32_kernel(RopeArgs a) {
   const uint32_t stride = gridDim.x * blockDim.x;
   for (uint32_t g0 = blockIdx.x * blockDim.x + threadIdx.x; g0 < total; g0 += U * stride) {
     uint4 xr[U];
-    float c[U][P], s[U][P];
+    CsRaw<CDT, P> c[U], s[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const uint32_t g = g0 + u * stride;
@@ -118,8 +131,8 @@ __global__ void __launch_bounds__(256) rope_vec32_kernel(RopeArgs a) {
         const uint32_t row = a.f_vpr.div(g);
         const uint32_t v = g - row * a.f_vpr.d;
         const uint32_t coff = a.f_rows.mod(a.f_div.div(row)) * half + v * P;
-        load_cs<CDT, P>(reinterpret_cast<const CT*>(a.cos) + coff, c[u]);
-        load_cs<CDT, P>(reinterpret_cast<const CT*>(a.sin) + coff, s[u]);
+        c[u].load(reinterpret_cast<const CT*>(a.cos) + coff);
+        s[u].load(reinterpret_cast<const CT*>(a.sin) + coff);
       }
     }
 #pragma unroll
@@ -131,8 +144,9 @@ __global__ void __launch_bounds__(256) rope_vec32_kernel(RopeArgs a) {
 #pragma unroll
       for (int q = 0; q < P; ++q) {
         const float x1 = E::to_f(e[2 * q]), x2 = E::to_f(e[2 * q + 1]);
-        o[2 * q] = fmaf(x1, c[u][q], -x2 * s[u][q]);
-        o[2 * q + 1] = fmaf(x1, s[u][q], x2 * c[u][q]);
+        const float cq = c[u].at(q), sq = s[u].at(q);
+        o[2 * q] = fmaf(x1, cq, -x2 * sq);
+        o[2 * q + 1] = fmaf(x1, sq, x2 * cq);
       }
       store_vec<DT>(reinterpret_cast<T*>(a.y) + (size_t)g * VEC, o);
     }
