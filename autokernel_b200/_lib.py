@@ -29,8 +29,8 @@ SIGNATURES = {
     "ak_sm_count": (_i32, []),
     "ak_set_force_simt": (None, [_i32]),
     "ak_set_gemm_pair": (None, [_i32]),
-    "ak_set_attn_pair": (None, [_i32]),
     "ak_rmsnorm": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
+    "ak_rmsnorm_fp32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
     "ak_layernorm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
     "ak_softmax": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp]),
     "ak_rotary_embedding": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),

@@ -30,14 +30,17 @@ int launch_status(const char* what) {
 
 __device__ int g_status = 0;
 
-static constexpr int kMaxDevices = 64;
 static DeviceInfo g_info[kMaxDevices];
 static std::once_flag g_once[kMaxDevices];
 
-const DeviceInfo& device_info() {
+int current_device() {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDevices) dev = 0;
+  return (dev < 0 || dev >= kMaxDevices) ? 0 : dev;
+}
+
+const DeviceInfo& device_info() {
+  const int dev = current_device();
   std::call_once(g_once[dev], [dev]() {
     DeviceInfo& d = g_info[dev];
     cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);

@@ -11,6 +11,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <mutex>
 #include <string>
 
 #include "../../include/ak_b200.h"
@@ -59,6 +60,20 @@ template <> struct Elem<AK_BF16> {
   static AK_D float to_f(T v) { return __bfloat162float(v); }
   static AK_D T from_f(float v) { return __float2bfloat16_rn(v); }
 };
+
+// Round two fp32 values to the storage dtype and back with one packed conversion.
+template <int DT>
+AK_D void rnd2(float& a, float& b) {
+  if constexpr (DT == AK_F16) {
+    const float2 r = __half22float2(__floats2half2_rn(a, b));
+    a = r.x;
+    b = r.y;
+  } else if constexpr (DT == AK_BF16) {
+    const float2 r = __bfloat1622float2(__floats2bfloat162_rn(a, b));
+    a = r.x;
+    b = r.y;
+  }
+}
 
 inline int dtype_size(int dt) { return dt == AK_F32 ? 4 : 2; }
 inline bool dtype_ok(int dt) { return dt == AK_F32 || dt == AK_F16 || dt == AK_BF16; }
@@ -172,5 +187,22 @@ struct DeviceInfo {
   int cc_major, cc_minor;
 };
 const DeviceInfo& device_info();  // cached per device, thread safe
+
+constexpr int kMaxDevices = 64;
+int current_device();  // the calling thread's current device, clamped to [0, kMaxDevices)
+
+// Opt `Kernel` into `bytes` of dynamic shared memory.  The attribute belongs to the
+// current device's context, so it is set once per (kernel, device) and the result kept
+// per device: a process that launches on cuda:0 and then cuda:1 sets it on both.
+template <auto Kernel>
+cudaError_t smem_optin(int bytes) {
+  static std::once_flag once[kMaxDevices];
+  static cudaError_t err[kMaxDevices];
+  const int dev = current_device();
+  std::call_once(once[dev], [dev, bytes] {
+    err[dev] = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  });
+  return err[dev];
+}
 
 }  // namespace ak

@@ -19,7 +19,5 @@ struct AttnShape {
 
 bool tc_attention_ok(const AttnShape& a);
 int tc_attention(const AttnShape& a, cudaStream_t s);
-// head_dim 128 on a CTA pair (cta_group::2); called by tc_attention
-int tc_attention_pair(const AttnShape& a, cudaStream_t s);
 
 }  // namespace ak

@@ -59,6 +59,7 @@ struct Params {
   int Sq, Sk, H, rep;        // rep = query heads per key/value head
   int causal;
   float scale_log2;  // sm_scale * log2(e)
+  float ovf;         // |raw score| at which reference.py's 16-bit scores overflow (inf: none)
   uint32_t idesc_qk, idesc_pv;
   int n_qblk;        // query blocks of 256 rows
 };
@@ -199,6 +200,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t t_s = tmem + x * C::TMEM_TILE + lane_base;
     const uint32_t t_o = t_s + 128;
     float m_ref = -INFINITY, l = 0.f;
+    float rmax_raw = -INFINITY;  // the row's largest visible raw score
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       int w = 0;
@@ -227,6 +229,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       float bmax = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 128; ++i) bmax = fmaxf(bmax, __uint_as_float(r[i]));
+      rmax_raw = fmaxf(rmax_raw, bmax);
       bmax *= p.scale_log2;
       // lazy rescale: move the reference max only when it grows by more than 8.  The
       // decision is per row (lane); the TMEM rescale of O is warp-collective, so the whole
@@ -284,7 +287,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     w = __shfl_sync(0xffffffffu, w, 0);
     if (w) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      // reference.py forms the scores in the input dtype: in fp16 a visible score beyond
+      // +-65504 (or one that leaves no finite key) turns the row's softmax into NaN there
+      const bool nan_row = rmax_raw >= p.ovf || rmax_raw <= -p.ovf;
+      const float inv = nan_row ? __int_as_float(0x7fffffff) : (l > 0.f ? 1.f / l : 0.f);
       T* orow = reinterpret_cast<T*>(p.O) + b * p.o_sb + h * p.o_sh + (int64_t)qrow * p.o_ss;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
@@ -345,16 +351,13 @@ static int launch(const AttnShape& a, cudaStream_t st) {
   p.rep = (int)(a.H / a.Hkv);
   p.causal = a.causal;
   p.scale_log2 = a.scale * 1.4426950408889634f;
+  // fp16 scores round to inf from 65520 on, before and after the scale (reference.py:36)
+  p.ovf = DT == AK_F16 ? 65520.f * fminf(1.f, 1.f / a.scale) : INFINITY;
   const int fmt = DT == AK_BF16 ? 1 : 0;
   p.idesc_qk = idesc_f16(fmt, BQ, BKV, false, false);
   p.idesc_pv = idesc_f16(fmt, BQ, D, false, true);
   p.n_qblk = (a.Sq + 2 * BQ - 1) / (2 * BQ);
-  static std::once_flag once;
-  static cudaError_t attr = cudaSuccess;
-  std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(attn_kernel<DT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                Cfg<D>::SMEM);
-  });
+  const cudaError_t attr = smem_optin<attn_kernel<DT, D>>(Cfg<D>::SMEM);
   AK_REQUIRE(attr == cudaSuccess, AK_ERR_LAUNCH, "attention smem attribute: %s",
              cudaGetErrorString(attr));
   dim3 grid((unsigned)p.n_qblk, (unsigned)(a.B * a.H));
@@ -379,19 +382,10 @@ bool tc_attention_ok(const AttnShape& a) {
   return device_info().cc_major == 10;
 }
 
-// The CTA-pair kernel is opt-in (ak_set_attn_pair / AK_ATTN_PAIR=1): it is correct and
-// pipelines Q K^T ahead of the softmax, but both kernels are bound by the softmax's
-// exponential throughput and the single-CTA one measured faster.
-int g_attn_pair = [] {
-  const char* e = getenv("AK_ATTN_PAIR");
-  return (e && e[0] == '1') ? 1 : 0;
-}();
-
 int tc_attention(const AttnShape& a, cudaStream_t s) {
   AK_REQUIRE(a.B * a.H <= 0x7fffffffLL, AK_ERR_SHAPE, "batch*heads too large");
   AK_REQUIRE(a.B * a.H <= 65535, AK_ERR_SHAPE, "batch*heads %lld exceeds 65535",
              (long long)(a.B * a.H));
-  if (a.D == 128 && g_attn_pair) return tc_attention_pair(a, s);
   if (a.dtype == AK_BF16) {
     if (a.D == 128) return attn::launch<AK_BF16, 128>(a, s);
     return attn::launch<AK_BF16, 64>(a, s);
@@ -402,4 +396,3 @@ int tc_attention(const AttnShape& a, cudaStream_t s) {
 
 }  // namespace ak
 
-extern "C" void ak_set_attn_pair(int on) { ak::g_attn_pair = on ? 1 : 0; }

@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            v[j] = apply_act(p.act, __uint_as_float(g[j])) * __uint_as_float(u[j]);
+            v[j] = swiglu_ref<DT>(p.act, __uint_as_float(g[j]), __uint_as_float(u[j]));
           store_row32<DT>(p, row, tn * (BN / 2) + c, v);
         }
       }
@@ -517,7 +517,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            v[j] = apply_act(p.act, __uint_as_float(g[j])) * __uint_as_float(u[j]);
+            v[j] = swiglu_ref<DT>(p.act, __uint_as_float(g[j]), __uint_as_float(u[j]));
           store_row32<DT>(p, row, tn * (BN / 2) + c, v);
         }
       }
@@ -582,12 +582,7 @@ static int launch(const void* A, const void* B, const void* B2, void* C, int M, 
   p.rope_cols = rope.cols;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, BM, BN, false, MODE == MODE_MN);
 
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_kernel<DT, MODE>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  });
+  const cudaError_t attr_err = smem_optin<gemm_kernel<DT, MODE>>(SMEM_BYTES);
   AK_REQUIRE(attr_err == cudaSuccess, AK_ERR_LAUNCH, "gemm: smem attribute: %s",
              cudaGetErrorString(attr_err));
   int grid = device_info().sm_count;
@@ -642,12 +637,7 @@ static int launch_pair(const void* A, const void* B, const void* B2, void* C, in
   p.rope_cols = rope.cols;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, 256, BN, false, MODE == MODE_MN);
 
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_pair_kernel<DT, MODE>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
-  });
+  const cudaError_t attr_err = smem_optin<gemm_pair_kernel<DT, MODE>>(P_SMEM_BYTES);
   AK_REQUIRE(attr_err == cudaSuccess, AK_ERR_LAUNCH, "gemm pair: smem attribute: %s",
              cudaGetErrorString(attr_err));
   int pairs = device_info().sm_count / 2;

@@ -10,8 +10,14 @@
 // Each thread handles 16-byte vectors of x (4 pairs in 16-bit types, 2 in
 // fp32) and the matching cos/sin pieces, four vectors in flight at a time, so x
 // is read once and y written once with 128-bit accesses; cos/sin (1 MB at
-// S=4096) stay in L2.  Arithmetic is
-// fp32 with a single rounding at the store.
+// S=4096) stay in L2.
+//
+// Rounding: when cos/sin have x's dtype (the kernel_fn / reference.py case) the arithmetic is
+// reference.py's operator sequence -- each product x * cos, x * sin rounded to the dtype, then
+// the difference / sum rounded -- so the output is bit-identical to reference.py (the products
+// of two 16-bit values are exact in fp32, and ATen rounds each one to the dtype).  With fp32
+// tables (the model path, models/llama_7b.py:40-48, which rotates in fp32) it is fp32
+// arithmetic with a single rounding at the store.
 #include "ak_common.cuh"
 
 #include <type_traits>
@@ -54,6 +60,22 @@ struct CsRaw {
   AK_D float at(int i) const { return Elem<CDT>::to_f(reinterpret_cast<const T*>(&w)[i]); }
 };
 
+// One rotated pair.  REF: reference.py's rounding (products rounded to the dtype, no fma
+// contraction); otherwise fp32 fmas.
+template <int DT, bool REF>
+AK_D void rope_pair(float x1, float x2, float c, float s, float& o1, float& o2) {
+  if constexpr (REF) {
+    float a = __fmul_rn(x1, c), b = __fmul_rn(x2, s), e = __fmul_rn(x1, s), f = __fmul_rn(x2, c);
+    rnd2<DT>(a, b);
+    rnd2<DT>(e, f);
+    o1 = __fsub_rn(a, b);
+    o2 = __fadd_rn(e, f);
+  } else {
+    o1 = fmaf(x1, c, -x2 * s);
+    o2 = fmaf(x1, s, x2 * c);
+  }
+}
+
 template <int DT, int CDT>
 __global__ void __launch_bounds__(256) rope_vec_kernel(RopeArgs a) {
   using E = Elem<DT>;
@@ -94,8 +116,7 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(RopeArgs a) {
 #pragma unroll
       for (int q = 0; q < P; ++q) {
         const float x1 = E::to_f(e[2 * q]), x2 = E::to_f(e[2 * q + 1]);
-        o[2 * q] = fmaf(x1, c[u][q], -x2 * s[u][q]);
-        o[2 * q + 1] = fmaf(x1, s[u][q], x2 * c[u][q]);
+        rope_pair<DT, CDT == DT>(x1, x2, c[u][q], s[u][q], o[2 * q], o[2 * q + 1]);
       }
       store_vec<DT>(reinterpret_cast<T*>(a.y) + g * VEC, o);
     }
@@ -144,9 +165,7 @@ __global__ void __launch_bounds__(256) rope_vec32_kernel(RopeArgs a) {
 #pragma unroll
       for (int q = 0; q < P; ++q) {
         const float x1 = E::to_f(e[2 * q]), x2 = E::to_f(e[2 * q + 1]);
-        const float cq = c[u].at(q), sq = s[u].at(q);
-        o[2 * q] = fmaf(x1, cq, -x2 * sq);
-        o[2 * q + 1] = fmaf(x1, sq, x2 * cq);
+        rope_pair<DT, CDT == DT>(x1, x2, c[u].at(q), s[u].at(q), o[2 * q], o[2 * q + 1]);
       }
       store_vec<DT>(reinterpret_cast<T*>(a.y) + (size_t)g * VEC, o);
     }
@@ -172,8 +191,10 @@ __global__ void __launch_bounds__(256) rope_scalar_kernel(RopeArgs a) {
     const float c = CE::to_f(reinterpret_cast<const CT*>(a.cos)[crow * half + p]);
     const float s = CE::to_f(reinterpret_cast<const CT*>(a.sin)[crow * half + p]);
     const float x1 = E::to_f(x[row * a.d + 2 * p]), x2 = E::to_f(x[row * a.d + 2 * p + 1]);
-    y[row * a.d + 2 * p] = E::from_f(fmaf(x1, c, -x2 * s));
-    y[row * a.d + 2 * p + 1] = E::from_f(fmaf(x1, s, x2 * c));
+    float o1, o2;
+    rope_pair<DT, CDT == DT>(x1, x2, c, s, o1, o2);
+    y[row * a.d + 2 * p] = E::from_f(o1);
+    y[row * a.d + 2 * p + 1] = E::from_f(o2);
   }
 }
 

@@ -5,10 +5,18 @@
 //   rmsnorm   y = (x / sqrt(mean(x^2) + eps)) * w          reference.py:26-29
 //   layernorm y = (x - mean) * rsqrt(var + eps) * w + b    reference.py:20-23 (F.layer_norm)
 //   softmax   y = exp(x - max) / sum(exp(x - max))         reference.py:15-17
-// all accumulated in fp32 with fixed-order (deterministic) reductions.  The
-// per-element divisions are applied as one reciprocal per row times a multiply
-// (at most one extra fp32 rounding, far below every output tolerance), which
-// keeps the ALU work under the HBM time.
+// all accumulated in fp32 with fixed-order (deterministic) reductions.
+//
+// RMSNorm comes in two roundings.  OP_RMS_REF is reference.py's operator sequence in the
+// input dtype: each of x*x, mean, + eps, sqrt, x / rms and * w is computed in fp32 and
+// rounded to the input dtype, as ATen's 16-bit elementwise ops do (the sum inside the mean
+// accumulates in fp32).  So it gives reference.py's results -- including its fp16 overflow
+// of x*x for |x| > 256, which zeroes the row -- up to the order of the fp32 sum.  OP_RMS is
+// the fp32 form x * (1 / sqrt(mean(x^2) + eps)) * w with one rounding at the end (the model
+// path, where that overflow would be a defect).  For LayerNorm and softmax the reference
+// rounds once (ATen computes them in fp32), and so do these kernels; their per-element
+// divisions are one reciprocal per row times a multiply (at most one extra fp32 rounding, far
+// below every output tolerance), which keeps the ALU work under the HBM time.
 //
 // Fast path: the whole row lives in registers as raw 128-bit vectors, so x is
 // read from HBM exactly once and y written once (the algorithmic 2*rows*cols
@@ -21,7 +29,34 @@
 
 namespace ak {
 
-enum RowOp { OP_RMS = 0, OP_LN = 1, OP_SOFTMAX = 2 };
+enum RowOp { OP_RMS = 0, OP_LN = 1, OP_SOFTMAX = 2, OP_RMS_REF = 3 };
+
+// Round an fp32 value to the storage dtype and back (identity for fp32).
+template <int DT>
+AK_D float rnd(float v) {
+  return Elem<DT>::to_f(Elem<DT>::from_f(v));
+}
+
+// a / b correctly rounded in fp32, from inv = 1 / b (rounded): q0 = a * inv carries at most
+// ~1.5 ulp of error, and one step on the exact remainder a - q0 * b (an fma) brings it to the
+// correctly rounded quotient -- the fp32 division ATen performs -- for the finite, normal
+// operands a normalisation sees, at 3 FMA-pipe operations instead of a full IEEE division.
+// With b = inf (an overflowed rms) or a = +-inf the remainder is NaN and q0 (a * 0 = 0, or
+// inf / NaN) is already the IEEE quotient.
+AK_D float div_rn(float a, float b, float inv) {
+  const float q0 = a * inv;
+  const float r = fmaf(-q0, b, a);
+  return r == r ? fmaf(r, inv, q0) : q0;
+}
+
+// rms of reference.py:26-29 from the fp32 sum of the rounded squares: mean = sum * (1 / n)
+// (ATen's mean multiplies by the fp32 reciprocal of the count), then + eps and sqrt, each
+// rounded to the dtype.
+template <int DT>
+AK_D float rms_ref(float sumsq, int64_t n, float eps) {
+  const float mean = rnd<DT>(sumsq * __frcp_rn((float)n));
+  return rnd<DT>(__fsqrt_rn(rnd<DT>(mean + eps)));
+}
 
 struct RowArgs {
   const void* x;
@@ -78,6 +113,22 @@ __global__ void __launch_bounds__(1024) row_reg_kernel(RowArgs a) {
     }
     acc = rsum(acc);
     s0 = 1.0f / sqrtf(acc / n + a.eps);  // 1 / rms
+  } else if (OP == OP_RMS_REF) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      float f[VEC];
+      elems(i, f);
+#pragma unroll
+      for (int j = 0; j < VEC; j += 2) {
+        float p = f[j] * f[j], q = f[j + 1] * f[j + 1];
+        rnd2<DT>(p, q);
+        acc += p + q;
+      }
+    }
+    acc = rsum(acc);
+    s0 = rms_ref<DT>(acc, a.cols, a.eps);  // rms, rounded like reference.py's
+    s1 = 1.0f / s0;
   } else if (OP == OP_LN) {
     float acc = 0.f;
 #pragma unroll
@@ -144,6 +195,16 @@ __global__ void __launch_bounds__(1024) row_reg_kernel(RowArgs a) {
       load_vec<DT>(w + v * VEC, wf);
 #pragma unroll
       for (int j = 0; j < VEC; ++j) o[j] = (f[j] * s0) * wf[j];
+    } else if (OP == OP_RMS_REF) {
+      float wf[VEC];
+      load_vec<DT>(w + v * VEC, wf);
+#pragma unroll
+      for (int j = 0; j < VEC; j += 2) {
+        float p = div_rn(f[j], s0, s1), q = div_rn(f[j + 1], s0, s1);
+        rnd2<DT>(p, q);
+        o[j] = p * wf[j];
+        o[j + 1] = q * wf[j + 1];
+      }
     } else if (OP == OP_LN) {
       float wf[VEC], bf[VEC];
       load_vec<DT>(w + v * VEC, wf);
@@ -181,6 +242,16 @@ __global__ void __launch_bounds__(512) row_loop_kernel(RowArgs a) {
     const float inv = 1.0f / sqrtf(block_sum(acc, red) / n + a.eps);
     for (int64_t c = threadIdx.x; c < a.cols; c += blockDim.x)
       yr[c] = E::from_f((E::to_f(xr[c]) * inv) * E::to_f(w[c]));
+  } else if (OP == OP_RMS_REF) {
+    float acc = 0.f;
+    for (int64_t c = threadIdx.x; c < a.cols; c += blockDim.x) {
+      float f = E::to_f(xr[c]);
+      acc += rnd<DT>(f * f);
+    }
+    const float rms = rms_ref<DT>(block_sum(acc, red), a.cols, a.eps);
+    const float inv = 1.0f / rms;
+    for (int64_t c = threadIdx.x; c < a.cols; c += blockDim.x)
+      yr[c] = E::from_f(rnd<DT>(div_rn(E::to_f(xr[c]), rms, inv)) * E::to_f(w[c]));
   } else if (OP == OP_LN) {
     float acc = 0.f;
     for (int64_t c = threadIdx.x; c < a.cols; c += blockDim.x) acc += E::to_f(xr[c]);
@@ -285,6 +356,17 @@ using namespace ak;
 
 extern "C" int ak_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t cols,
                           int64_t ldx, int64_t ldy, float eps, int dtype, void* stream) {
+  int rc = check_rows(x, y, rows, cols, ldx, ldy, dtype);
+  if (rc) return rc;
+  if (rows == 0 || cols == 0) return AK_OK;
+  AK_REQUIRE(w, AK_ERR_ARG, "rmsnorm: null weight");
+  RowArgs a{x, w, nullptr, y, rows, cols, ldx, ldy, eps};
+  return dispatch_rowop<OP_RMS_REF>(a, dtype, (cudaStream_t)stream);
+}
+
+extern "C" int ak_rmsnorm_fp32(const void* x, const void* w, void* y, int64_t rows,
+                               int64_t cols, int64_t ldx, int64_t ldy, float eps, int dtype,
+                               void* stream) {
   int rc = check_rows(x, y, rows, cols, ldx, ldy, dtype);
   if (rc) return rc;
   if (rows == 0 || cols == 0) return AK_OK;

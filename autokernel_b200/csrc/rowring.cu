@@ -223,12 +223,7 @@ static int dispatch(const RingArgs& a, cudaStream_t st) {
   if (L.stages < 3) return 1;
   L.nvt = (int)((a.cols / VEC + TPG - 1) / TPG);
   if (L.nvt > MAX_NVT) return 1;
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, [] {
-    err = cudaFuncSetAttribute(ring_kernel<DT, OP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               SMEM_BUDGET);
-  });
+  const cudaError_t err = smem_optin<ring_kernel<DT, OP>>(SMEM_BUDGET);
   AK_REQUIRE(err == cudaSuccess, AK_ERR_LAUNCH, "ring smem attribute: %s", cudaGetErrorString(err));
   int grid = device_info().sm_count;
   if (grid > a.rows) grid = (int)a.rows;

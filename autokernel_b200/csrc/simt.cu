@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const void* Av, const vo
       const int gn = n0 + tx * 4 + j;
       if (gn >= N) continue;
       float v = acc[i][j];
-      if (DUAL) v = apply_act(act, v) * acc2[i][j];
+      if (DUAL) v = swiglu_ref<DT>(act, v, acc2[i][j]);
       if (Rv) v += E::to_f(reinterpret_cast<const T*>(Rv)[(int64_t)gm * ldr + gn]);
       C[(int64_t)gm * ldc + gn] = E::from_f(v);
     }

@@ -11,7 +11,7 @@ module surgery (verify.py:510-641), extended to attention, RoPE, the MLP and the
 loss.
 
 Every arithmetic step is one of this package's kernels:
-    RMSNorm              ops.rmsnorm           (csrc/rowops.cu)
+    RMSNorm              ops.rmsnorm_fp32      (csrc/rowops.cu, fp32 intermediates)
     q/k/v/o projections  ops.linear            (tcgen05 GEMM, K-major weights, no copies)
     RoPE                 ops.rope_apply        (fp32 cos/sin table, [B, T, H, D] in place)
     attention            ops.attention_bhsd    (reads [B, T, H, D] views, GQA, causal)
@@ -120,7 +120,7 @@ class LlamaB200:
         p = f"layers.{i}."
         B, T, _ = h.shape
         hd = c.head_dim
-        x = ops.rmsnorm(h, w[p + "attention_norm.weight"], c.norm_eps)
+        x = ops.rmsnorm_fp32(h, w[p + "attention_norm.weight"], c.norm_eps)
         q = ops.linear(x, w[p + "attention.wq.weight"]).view(B, T, c.n_heads, hd)
         k = ops.linear(x, w[p + "attention.wk.weight"]).view(B, T, c.n_kv_heads, hd)
         v = ops.linear(x, w[p + "attention.wv.weight"]).view(B, T, c.n_kv_heads, hd)
@@ -137,7 +137,7 @@ class LlamaB200:
             o = o.transpose(1, 2).contiguous()
         # residual adds happen in the GEMM epilogues, in place on h
         ops.linear(o.view(B, T, c.n_heads * hd), w[p + "attention.wo.weight"], residual=h, out=h)
-        x = ops.rmsnorm(h, w[p + "ffn_norm.weight"], c.norm_eps)
+        x = ops.rmsnorm_fp32(h, w[p + "ffn_norm.weight"], c.norm_eps)
         hidden = ops.mlp_hidden(x, w[p + "feed_forward.w1.weight"], w[p + "feed_forward.w3.weight"])
         ops.linear(hidden, w[p + "feed_forward.w2.weight"], residual=h, out=h)
         return h
@@ -150,7 +150,7 @@ class LlamaB200:
         h = torch.nn.functional.embedding(tokens, self.w["tok_embeddings.weight"])  # new tensor
         for i in range(self.cfg.n_layers):
             h = self._layer(i, h, cos, sin)
-        h = ops.rmsnorm(h, self.w["norm.weight"], self.cfg.norm_eps)
+        h = ops.rmsnorm_fp32(h, self.w["norm.weight"], self.cfg.norm_eps)
         return ops.linear(h, self.w["output.weight"])
 
     __call__ = forward

@@ -58,12 +58,23 @@ def _same_dtype(x: torch.Tensor, *ps: torch.Tensor) -> list[torch.Tensor]:
 # ---------------------------------------------------------------- row ops
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
-    """y = x / sqrt(mean(x^2, -1) + eps) * weight (reference.py:26-29)."""
+    """y = x / sqrt(mean(x^2, -1) + eps) * weight (reference.py:26-29), each step rounded to
+    x's dtype as reference.py rounds it."""
+    return _rmsnorm("ak_rmsnorm", x, weight, eps)
+
+
+def rmsnorm_fp32(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """y = x * rsqrt(mean(x^2, -1) + eps) * weight with fp32 intermediates and one rounding
+    (models/llama_7b.py:22-30 RMSNorm without the 16-bit overflow of x^2)."""
+    return _rmsnorm("ak_rmsnorm_fp32", x, weight, eps)
+
+
+def _rmsnorm(entry: str, x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     require_cuda(x, weight)
     (weight,) = _same_dtype(x, weight.contiguous())
     x2 = _rows_view(x)
     y = torch.empty(x2.shape, dtype=x.dtype, device=x.device)
-    call("ak_rmsnorm", x2.data_ptr(), weight.data_ptr(), y.data_ptr(), x2.shape[0], x2.shape[1],
+    call(entry, x2.data_ptr(), weight.data_ptr(), y.data_ptr(), x2.shape[0], x2.shape[1],
          x2.stride(0), y.stride(0), float(eps), dtype_code(x.dtype), stream_ptr(x.device))
     return y.view(x.shape)
 

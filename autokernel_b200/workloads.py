@@ -37,27 +37,43 @@ SWEEP = {
 }
 
 
-def sweep_inputs(device, seed: int = 0, scale: float = 1.0) -> dict:
+SWEEP_BLOCKS = 8  # configs[1] is cut into 8 equal blocks along its sharded (row / batch) dim
+
+
+def sweep_inputs(device, blocks=range(SWEEP_BLOCKS), seed: int = 0, scale: float = 1.0) -> dict:
     """softmax x~N(0, sd 2) [8192, 32768]; LayerNorm x~N(0,1) [16384, 4096] with
     w = 1 + 0.1N, b = 0.1N, eps 1e-5; RoPE q, k ~N(0,1) [8, 32, 4096, 128] with theta 10000;
-    reduce x~U(-1,1) fp32 [2^30].  bf16 except reduce.  `scale` < 1 shrinks the leading dims
-    (used for small profiling captures)."""
-    g = _gen(device, seed)
+    reduce x~U(-1,1) fp32 [2^30].  bf16 except reduce.
+
+    The full configuration is SWEEP_BLOCKS blocks of rows (softmax 1024 rows, LayerNorm 2048
+    rows, RoPE one batch entry, reduce 2^27 elements); block b is drawn from its own generator
+    seeded with seed + b, so a rank that owns blocks [b0, b1) holds exactly rows [b0, b1) of
+    the one global tensor whatever the number of GPUs.  Blocks past SWEEP_BLOCKS continue the
+    same sequence (a weak-scaled run gives rank r the blocks [8r, 8r + 8)).  `scale` < 1
+    shrinks every block (small profiling captures only)."""
+    blocks = list(blocks)
+    nb = len(blocks)
     bf = torch.bfloat16
     s, l, r, rd = SWEEP["softmax"], SWEEP["layernorm"], SWEEP["rope"], SWEEP["reduce"]
-    sr = max(1, int(s["rows"] * scale))
-    lr = max(1, int(l["rows"] * scale))
-    rb = max(1, int(r["B"] * scale))
-    n = max(1024, int(rd["n"] * scale))
+    per = lambda n: max(1, int(n // SWEEP_BLOCKS * scale))  # noqa: E731
+    sr, lr, rb, n = per(s["rows"]), per(l["rows"]), per(r["B"]), max(1024, per(rd["n"]))
     d = {
-        "sm_x": (torch.randn(sr, s["cols"], device=device, generator=g) * 2.0).to(bf),
-        "ln_x": torch.randn(lr, l["cols"], device=device, generator=g).to(bf),
-        "ln_w": (1 + 0.1 * torch.randn(l["cols"], device=device, generator=g)).to(bf),
-        "ln_b": (0.1 * torch.randn(l["cols"], device=device, generator=g)).to(bf),
-        "q": torch.randn(rb, r["H"], r["S"], r["D"], device=device, generator=g).to(bf),
-        "k": torch.randn(rb, r["H"], r["S"], r["D"], device=device, generator=g).to(bf),
-        "red_x": torch.rand(n, device=device, generator=g) * 2 - 1,
+        "sm_x": torch.empty(nb * sr, s["cols"], device=device, dtype=bf),
+        "ln_x": torch.empty(nb * lr, l["cols"], device=device, dtype=bf),
+        "q": torch.empty(nb * rb, r["H"], r["S"], r["D"], device=device, dtype=bf),
+        "k": torch.empty(nb * rb, r["H"], r["S"], r["D"], device=device, dtype=bf),
+        "red_x": torch.empty(nb * n, device=device, dtype=torch.float32),
     }
+    for i, b in enumerate(blocks):
+        g = _gen(device, seed + b)
+        d["sm_x"][i * sr:(i + 1) * sr] = torch.randn(sr, s["cols"], device=device, generator=g) * 2.0
+        d["ln_x"][i * lr:(i + 1) * lr] = torch.randn(lr, l["cols"], device=device, generator=g)
+        d["q"][i * rb:(i + 1) * rb] = torch.randn(rb, r["H"], r["S"], r["D"], device=device, generator=g)
+        d["k"][i * rb:(i + 1) * rb] = torch.randn(rb, r["H"], r["S"], r["D"], device=device, generator=g)
+        d["red_x"][i * n:(i + 1) * n] = torch.rand(n, device=device, generator=g) * 2 - 1
+    g = _gen(device, seed + 1_000_003)  # parameters shared by every block
+    d["ln_w"] = (1 + 0.1 * torch.randn(l["cols"], device=device, generator=g)).to(bf)
+    d["ln_b"] = (0.1 * torch.randn(l["cols"], device=device, generator=g)).to(bf)
     d["cos"], d["sin"] = rope_table(r["S"], r["D"] // 2, device=device)
     return d
 

@@ -122,10 +122,16 @@ def barrier(world, device):
 
 # ------------------------------------------------------------------ our arm
 
-def run_sweep_step(d, ev=None):
-    """One step of the headline workload through the public ops API."""
-    from autokernel_b200 import ops, shard
+def run_sweep_step(d, ev=None, world: int = 1):
+    """One step of the headline workload through the public ops API.  The sum runs first:
+    its fp64 partial is all-reduced over NCCL (N > 1) on NCCL's own stream while softmax,
+    LayerNorm and RoPE run, and the compute stream waits for it only before the final cast."""
+    from autokernel_b200 import ops
     out = {}
+    if ev: ev["reduce"][0].record()
+    total = ops.reduce_partial(d["red_x"])
+    if ev: ev["reduce"][1].record()
+    work = dist.all_reduce(total, op=dist.ReduceOp.SUM, async_op=True) if world > 1 else None
     if ev: ev["softmax"][0].record()
     out["sm"] = ops.softmax(d["sm_x"])
     if ev: ev["softmax"][1].record(); ev["layernorm"][0].record()
@@ -133,12 +139,64 @@ def run_sweep_step(d, ev=None):
     if ev: ev["layernorm"][1].record(); ev["rope"][0].record()
     out["q"] = ops.rotary_embedding(d["q"], d["cos"], d["sin"])
     out["k"] = ops.rotary_embedding(d["k"], d["cos"], d["sin"])
-    if ev: ev["rope"][1].record(); ev["reduce"][0].record()
-    total = ops.reduce_partial(d["red_x"])
-    if ev: ev["reduce"][1].record()
-    out["sum"] = shard.reduce_sum_sharded(d["red_x"], partial_fn=lambda _x: total,
-                                          out_dtype=torch.float32)
+    if ev: ev["rope"][1].record()
+    if work is not None:
+        work.wait()  # the compute stream (not the host) waits for the all-reduce
+    out["sum"] = ops.scalar_from_total(total, torch.float32)
+    out["total"] = total
     return out
+
+
+def time_steps(d, device, world, steps: int, warmup: int, bytes_per: dict | None = None):
+    """Warm-up, then `steps` timed steps between barriers; ms per step is the max over ranks.
+    With bytes_per, per-op CUDA events give each kernel's time and GB/s."""
+    for _ in range(warmup):
+        run_sweep_step(d, world=world)
+    ev_steps = ([{k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for k in bytes_per} for _ in range(steps)] if bytes_per else [None] * steps)
+    torch.cuda.synchronize()
+    barrier(world, device)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(device.index) as clk:
+        start.record()
+        for i in range(steps):
+            out = run_sweep_step(d, ev_steps[i], world=world)
+        stop.record()
+        torch.cuda.synchronize()
+    barrier(world, device)
+    torch.cuda.synchronize()
+    from autokernel_b200 import shard
+    ms = shard.max_over_ranks(start.elapsed_time(stop) / steps, device=device)
+    per_op = {}
+    if bytes_per:
+        pk = peaks()
+        for k in bytes_per:
+            t = sum(e[k][0].elapsed_time(e[k][1]) for e in ev_steps) / steps  # ms per launch
+            gbs = bytes_per[k] / (t * 1e-3) / 1e9
+            per_op[k] = {"us": t * 1e3, "GB/s": gbs, "frac_hbm": gbs / pk["hbm_gbs"],
+                         "bytes": bytes_per[k]}
+    return ms, per_op, clk.summary(), float(out["total"].item())
+
+
+def time_allreduce(device, world, reps: int = 200) -> dict | None:
+    """Device time of one NCCL all-reduce of the 8-byte fp64 partial the sum exchanges."""
+    if world <= 1:
+        return None
+    from autokernel_b200 import shard
+    t = torch.zeros(1, dtype=torch.float64, device=device)
+    for _ in range(10):
+        dist.all_reduce(t)
+    torch.cuda.synchronize()
+    barrier(world, device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        dist.all_reduce(t)
+    b.record()
+    torch.cuda.synchronize()
+    us = shard.max_over_ranks(a.elapsed_time(b) / reps * 1e3, device=device)
+    return {"us": round(us, 2), "bytes": 8, "nvls": os.environ.get("NCCL_NVLS_ENABLE", "default")}
 
 
 KERNELS_PER_STEP = 7  # softmax, layernorm, rope x2, reduce partial + final, scalar cast
@@ -150,9 +208,10 @@ def time_compute_ops(device, world, reps: int) -> dict:
     pk = peaks()
     res = {}
 
-    def timeit(fn, n=reps, warm=2):
-        """Seconds per call of fn: n calls captured once in a CUDA graph and replayed, so
-        small kernels are timed without the per-call Python / launch overhead."""
+    def timeit(fn, n=reps, warm=2, min_seconds=0.4):
+        """(seconds per call, clocks): n calls captured once in a CUDA graph, so small kernels
+        are timed without the per-call Python / launch overhead; the graph is replayed for at
+        least min_seconds with nvidia-smi sampling the SM clock during the timed replays."""
         for _ in range(warm):
             fn()
         torch.cuda.synchronize()
@@ -167,8 +226,16 @@ def time_compute_ops(device, world, reps: int) -> dict:
         g.replay()
         b.record()
         torch.cuda.synchronize()
+        loops = max(1, math.ceil(min_seconds / (a.elapsed_time(b) / 1e3)))
+        with Clocks(device.index) as clk:
+            a.record()
+            for _ in range(loops):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize()
         del g
-        return a.elapsed_time(b) / n / 1e3  # seconds
+        ck = clk.summary()
+        return a.elapsed_time(b) / loops / n / 1e3, {k: ck.get(k) for k in ("sm_mhz", "reasons", "samples")}
 
     g = torch.Generator(device=device).manual_seed(1)
     # RMSNorm configs[0] shape, fp16 with fp32 accumulation
@@ -177,25 +244,25 @@ def time_compute_ops(device, world, reps: int) -> dict:
     # 33.5 MB of input would sit in the 126 MB L2 between calls: rotate over 4 copies
     xs = [x] + [x.clone() for _ in range(3)]
     cyc = iter(range(1 << 30))
-    t = timeit(lambda: ops.rmsnorm(xs[next(cyc) % 4], w, 1e-6), n=max(reps, 48))
+    t, ck = timeit(lambda: ops.rmsnorm(xs[next(cyc) % 4], w, 1e-6), n=max(reps, 48))
     del xs
     by = 2 * x.numel() * 2 + w.numel() * 2
-    res["rmsnorm_fp16_4096x4096"] = {"GB/s": by / t / 1e9, "frac_hbm": by / t / 1e9 / pk["hbm_gbs"], "us": t * 1e6,
+    res["rmsnorm_fp16_4096x4096"] = {"clocks": ck, "GB/s": by / t / 1e9, "frac_hbm": by / t / 1e9 / pk["hbm_gbs"], "us": t * 1e6,
                                      "timing": "CUDA graph of 48 calls, inputs rotated over 4 buffers (134 MB > L2)"}
     del x, w
     # cross entropy: LM-head shard at 8 GPUs, fp16 logits
     lg = torch.randn(W.XENT["rows"], W.XENT["vocab"], device=device, generator=g).half()
     tg = torch.randint(0, W.XENT["vocab"], (W.XENT["rows"],), device=device, generator=g)
-    t = timeit(lambda: ops.cross_entropy(lg, tg))
+    t, ck = timeit(lambda: ops.cross_entropy(lg, tg))
     by = lg.numel() * 2 + tg.numel() * 8
-    res["cross_entropy_fp16_8192x32000"] = {"GB/s": by / t / 1e9, "frac_hbm": by / t / 1e9 / pk["hbm_gbs"], "us": t * 1e6}
+    res["cross_entropy_fp16_8192x32000"] = {"clocks": ck, "GB/s": by / t / 1e9, "frac_hbm": by / t / 1e9 / pk["hbm_gbs"], "us": t * 1e6}
     del lg, tg
     # GEMMs
     for (M, N, K) in W.GEMM_SHAPES:
         A, B = W.gemm_inputs(M, N, K, device)
-        t = timeit(lambda: ops.matmul(A, B), n=max(3, reps // 4))
+        t, ck = timeit(lambda: ops.matmul(A, B), n=max(3, reps // 4))
         tf = 2.0 * M * N * K / t / 1e12
-        res[f"matmul_bf16_{M}x{N}x{K}"] = {"TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "frac_tensor_sustained": tf / pk["bf16_tflops_sustained"], "ms": t * 1e3}
+        res[f"matmul_bf16_{M}x{N}x{K}"] = {"clocks": ck, "TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "frac_tensor_sustained": tf / pk["bf16_tflops_sustained"], "ms": t * 1e3}
         del A, B
     torch.cuda.empty_cache()
     # fused MLP
@@ -204,17 +271,17 @@ def time_compute_ops(device, world, reps: int) -> dict:
     wg = (torch.randn(m["H"], m["D"], device=device, generator=g) * 0.02).bfloat16()
     wu = (torch.randn(m["H"], m["D"], device=device, generator=g) * 0.02).bfloat16()
     wd = (torch.randn(m["D"], m["H"], device=device, generator=g) * 0.02).bfloat16()
-    t = timeit(lambda: ops.fused_mlp(xm, wg, wu, wd), n=max(3, reps // 4))
+    t, ck = timeit(lambda: ops.fused_mlp(xm, wg, wu, wd), n=max(3, reps // 4))
     tf = 6.0 * m["M"] * m["D"] * m["H"] / t / 1e12
-    res["fused_mlp_bf16_16384x4096x11008"] = {"TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "frac_tensor_sustained": tf / pk["bf16_tflops_sustained"], "ms": t * 1e3}
+    res["fused_mlp_bf16_16384x4096x11008"] = {"clocks": ck, "TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "frac_tensor_sustained": tf / pk["bf16_tflops_sustained"], "ms": t * 1e3}
     del xm, wg, wu, wd
     torch.cuda.empty_cache()
     # causal attention
     a = W.ATTN
     Q, K_, V = (torch.randn(a["B"], a["H"], a["S"], a["D"], device=device, generator=g).bfloat16() for _ in range(3))
-    t = timeit(lambda: ops.flash_attention(Q, K_, V, causal=True), n=max(2, reps // 8), warm=1)
+    t, ck = timeit(lambda: ops.flash_attention(Q, K_, V, causal=True), n=max(2, reps // 8), warm=1)
     tf = W.attn_flops(a["B"], a["H"], a["S"], a["D"]) / t / 1e12
-    res["flash_attention_bf16_causal_8x32x4096x128"] = {"TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "frac_tensor_sustained": tf / pk["bf16_tflops_sustained"], "ms": t * 1e3}
+    res["flash_attention_bf16_causal_8x32x4096x128"] = {"clocks": ck, "TFLOP/s": tf, "frac_tensor": tf / pk["bf16_tflops"], "frac_tensor_sustained": tf / pk["bf16_tflops_sustained"], "ms": t * 1e3}
     del Q, K_, V
     torch.cuda.empty_cache()
     return res
@@ -227,9 +294,14 @@ def time_llama(device, world, batch: int = 32, seq: int = 2048, reps: int = 2) -
     from autokernel_b200 import llama as L, shard
     cfg = L.LLAMA_7B
     m = L.LlamaB200(cfg, L.LlamaB200.random_weights(cfg, device, dtype=torch.float16, seed=0))
-    local = batch // world
-    g = torch.Generator(device=device).manual_seed(100 + (dist.get_rank() if world > 1 else 0))
-    tokens = torch.randint(0, cfg.vocab_size, (local, seq), device=device, generator=g)
+    # one global batch from one seed on every rank; rank r takes its contiguous sequences, so
+    # the loss (all-reduced mean over all 32 sequences) is computed on the same tokens at any N
+    from autokernel_b200 import shard as S
+    g = torch.Generator(device=device).manual_seed(100)
+    all_tokens = torch.randint(0, cfg.vocab_size, (batch, seq), device=device, generator=g)
+    r0, r1 = S.row_range(batch, dist.get_rank() if world > 1 else 0, world)
+    tokens = all_tokens[r0:r1].contiguous()
+    del all_tokens
     loss = m.loss(tokens)
     torch.cuda.synchronize()
     barrier(world, device)
@@ -244,6 +316,8 @@ def time_llama(device, world, batch: int = 32, seq: int = 2048, reps: int = 2) -
     flops = L.model_flops(cfg, batch, seq)
     tf = flops / world / (ms * 1e-3) / 1e12
     out = {"tok/s": batch * seq / (ms * 1e-3), "ms_per_fwd": ms, "loss": float(loss.float()),
+           "tokens": f"one global [{batch}, {seq}] batch (seed 100) sliced by rank, so the loss is "
+                     "over the same tokens at every N",
            "TFLOP/s_per_gpu": tf, "frac_tensor": tf / peaks()["bf16_tflops_sustained"],
            "peak_used": "bf16_tflops_sustained (measured)",
            "config": "32 layers, d 4096, 32 heads x 128 (MHA), ffn 11008, vocab 32000, fp16, "
@@ -322,41 +396,23 @@ def e2e_sweep(d, device, world, steps: int) -> dict:
 
 
 def ours(args):
-    from autokernel_b200 import ops, shard, workloads as W  # noqa: F401
+    from autokernel_b200 import shard, workloads as W
     rank, local, world = setup(args)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
+        # the only collectives are all-reduces of 8- and 16-byte fp64 partials: latency-bound,
+        # so NVLink SHARP (NVLS) multicast buffers buy nothing here
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", device_id=device)
-    pk = peaks()
-    d = W.sweep_inputs(device, seed=rank, scale=args.scale)
+    nb = W.SWEEP_BLOCKS
+    # headline, weak-scaled: rank r owns blocks [8r, 8r + 8) of one global block sequence, a
+    # full configs[1] shard; at N = 1 that is exactly the configs[1] tensors
+    d = W.sweep_inputs(device, blocks=range(nb * rank, nb * (rank + 1)), scale=args.scale)
     bytes_per = W.sweep_bytes(d)
     step_bytes = sum(bytes_per.values())
     torch.cuda.synchronize()
-
-    for _ in range(args.warmup):
-        run_sweep_step(d)
-    ev_steps = [{k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                 for k in bytes_per} for _ in range(args.steps)]
-    torch.cuda.synchronize()
-    barrier(world, device)
-    torch.cuda.synchronize()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clk:
-        start.record()
-        for i in range(args.steps):
-            run_sweep_step(d, ev_steps[i])
-        stop.record()
-        torch.cuda.synchronize()
-    barrier(world, device)
-    torch.cuda.synchronize()
-    ms_local = start.elapsed_time(stop) / args.steps
-    ms = shard.max_over_ranks(ms_local, device=device)
-    per_op = {}
-    for k in bytes_per:
-        t = sum(e[k][0].elapsed_time(e[k][1]) for e in ev_steps) / args.steps  # ms per launch
-        gbs = bytes_per[k] / (t * 1e-3) / 1e9
-        per_op[k] = {"us": t * 1e3, "GB/s": gbs, "frac_hbm": gbs / pk["hbm_gbs"], "bytes": bytes_per[k]}
+    ms, per_op, clocks, _ = time_steps(d, device, world, args.steps, args.warmup, bytes_per)
     value = world * step_bytes / (ms * 1e-3) / 1e9
 
     e2e = None
@@ -365,6 +421,27 @@ def ours(args):
         e2e = {"value": world * step_bytes / (r["ms_per_step"] * 1e-3) / 1e9, "unit": UNIT,
                "ms_per_step": r["ms_per_step"], "h2d_bytes_per_step": r["h2d"],
                "d2h_bytes_per_step": r["d2h"], "api": "autokernel_b200.ops (kernel_fn signatures)"}
+    # strong-scaled: the one configs[1] workload (blocks 0..7) split over the ranks, each rank
+    # its contiguous blocks; the global sum is printed so runs at different N can be compared
+    if world > 1:
+        del d
+        torch.cuda.empty_cache()
+        b0, b1 = shard.row_range(nb, rank, world)
+        d = W.sweep_inputs(device, blocks=range(b0, b1), scale=args.scale)
+    sbytes = shard.max_over_ranks(float(sum(W.sweep_bytes(d).values())), device=device)
+    s_ms, _, s_clk, s_total = time_steps(d, device, world, args.steps, args.warmup)
+    global_bytes = step_bytes if world == 1 else None
+    if world > 1:
+        t = torch.tensor([float(sum(W.sweep_bytes(d).values()))], dtype=torch.float64, device=device)
+        dist.all_reduce(t)
+        global_bytes = float(t.item())
+    strong = {"value": round(global_bytes / (s_ms * 1e-3) / 1e9, 1), "unit": UNIT,
+              "ms_per_step": round(s_ms, 4), "global_bytes_per_step": global_bytes,
+              "max_rank_bytes_per_step": sbytes, "blocks_per_rank": f"{nb // world if nb % world == 0 else 'uneven'}",
+              "global_sum_of_reduce": s_total, "clocks": s_clk,
+              "note": "configs[1] at its stated size (rows/batch sharded over the N GPUs); the "
+                      "global sum is the same number at every N up to fp64 rounding"}
+    allreduce = time_allreduce(device, world)
     del d
     torch.cuda.empty_cache()
     ops_res = None
@@ -378,7 +455,7 @@ def ours(args):
             ops_res = {**(ops_res or {}), "llama7b_fwd_ce": llama_res}
     cpu = None
     if not args.no_cpu and rank == 0 and world == 1:
-        cpu = cpu_baseline(args.cpu_seconds)
+        cpu = cpu_baseline(args.cpu_reps)
     if world > 1:
         dist.barrier(device_ids=[local])
 
@@ -388,7 +465,7 @@ def ours(args):
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16 (reduce: fp32 in, fp64 partials)", "data": "synthetic (seeded, device-generated)",
+        "dtype": "bf16 (reduce: fp32 in, fp64 partials)", "data": "synthetic (seeded, device-generated; block b of the global sequence drawn from seed b, so every N sees the same rows)",
         "config": {"workload": "configs[1] memory-bound sweep per GPU: softmax bf16 [8192,32768] N(0,sd2); "
                                "layernorm bf16 [16384,4096] eps1e-5; rope bf16 q,k [8,32,4096,128] theta1e4; "
                                "reduce fp32 [2^30] U(-1,1) + fp64 allreduce",
@@ -401,8 +478,11 @@ def ours(args):
                      "traffic": traffic, "algorithmic_bytes": bytes_per[dom]},
         "ops": {"sweep": per_op, **({"compute": ops_res} if ops_res else {})},
         "gpu_launches": KERNELS_PER_STEP * args.steps,
-        "clocks": clk.summary(),
+        "clocks": clocks,
+        "strong_scaling": strong,
     }
+    if allreduce:
+        line["allreduce_fp64_scalar"] = allreduce
     if e2e:
         line["e2e"] = e2e
     if cpu:
@@ -426,26 +506,41 @@ def traffic_from_profile(kernel: str):
 
 # ------------------------------------------------------------------ CPU baseline / reference arm
 
-def _cpu_sample():
-    """Bounded CPU sample of the sweep: same distributions, fewer rows."""
-    g = torch.Generator().manual_seed(0)
+def _cpu_inputs():
+    """configs[1] at its full size on the host (same shapes and distributions as the GPU arm,
+    drawn block by block from CPU generators): softmax [8192, 32768], LayerNorm [16384, 4096],
+    RoPE q, k [8, 32, 4096, 128], reduce fp32 [2^30]."""
+    from autokernel_b200 import workloads as W
     bf = torch.bfloat16
-    d = {
-        "sm_x": (torch.randn(1024, 32768, generator=g) * 2).to(bf),
-        "ln_x": torch.randn(4096, 4096, generator=g).to(bf),
-        "ln_w": (1 + 0.1 * torch.randn(4096, generator=g)).to(bf),
-        "ln_b": (0.1 * torch.randn(4096, generator=g)).to(bf),
-        "q": torch.randn(1, 32, 4096, 128, generator=g).to(bf),
-        "k": torch.randn(1, 32, 4096, 128, generator=g).to(bf),
-        "red_x": torch.rand(1 << 27, generator=g) * 2 - 1,
-    }
-    inv = 1.0 / 10000.0 ** (torch.arange(0, 128, 2).float() / 128)
-    ang = torch.outer(torch.arange(4096).float(), inv)
-    d["cos"], d["sin"] = ang.cos().to(bf), ang.sin().to(bf)
+    s, l, r, rd = W.SWEEP["softmax"], W.SWEEP["layernorm"], W.SWEEP["rope"], W.SWEEP["reduce"]
+    nb = W.SWEEP_BLOCKS
+    d = {"sm_x": torch.empty(s["rows"], s["cols"], dtype=bf),
+         "ln_x": torch.empty(l["rows"], l["cols"], dtype=bf),
+         "q": torch.empty(r["B"], r["H"], r["S"], r["D"], dtype=bf),
+         "k": torch.empty(r["B"], r["H"], r["S"], r["D"], dtype=bf),
+         "red_x": torch.empty(rd["n"], dtype=torch.float32)}
+    for b in range(nb):
+        g = torch.Generator().manual_seed(b)
+        for key, scale, rows in (("sm_x", 2.0, s["rows"] // nb), ("ln_x", 1.0, l["rows"] // nb),
+                                 ("q", 1.0, r["B"] // nb), ("k", 1.0, r["B"] // nb)):
+            blk = d[key][b * rows:(b + 1) * rows]
+            blk.copy_(torch.randn(blk.shape, generator=g) * scale)
+        n = rd["n"] // nb
+        d["red_x"][b * n:(b + 1) * n] = torch.rand(n, generator=g) * 2 - 1
+    g = torch.Generator().manual_seed(1_000_003)
+    d["ln_w"] = (1 + 0.1 * torch.randn(l["cols"], generator=g)).to(bf)
+    d["ln_b"] = (0.1 * torch.randn(l["cols"], generator=g)).to(bf)
+    d["cos"], d["sin"] = W.rope_table(r["S"], r["D"] // 2, device="cpu")
     e = lambda t: t.numel() * t.element_size()  # noqa: E731
     nbytes = (2 * e(d["sm_x"]) + 2 * e(d["ln_x"]) + e(d["ln_w"]) + e(d["ln_b"]) + 4 * e(d["q"])
               + e(d["cos"]) + e(d["sin"]) + e(d["red_x"]))
     return d, nbytes
+
+
+CPU_SAMPLE = ("configs[1] at full size, the same workload as the GPU arm's config: "
+              "softmax bf16 [8192,32768], layernorm bf16 [16384,4096], rope bf16 q,k [8,32,4096,128], "
+              "reduce fp32 [2^30]; reference.py's operators on CPU tensors (oracle/ref_torch.py, "
+              "pinned bit for bit to reference.py)")
 
 
 def _cpu_step(d):
@@ -457,22 +552,18 @@ def _cpu_step(d):
     R.reduce_sum(d["red_x"], -1)
 
 
-def cpu_baseline(seconds: float) -> dict:
+def cpu_baseline(reps: int) -> dict:
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    d, nbytes = _cpu_sample()
+    d, nbytes = _cpu_inputs()
     _cpu_step(d)
     t0 = time.perf_counter()
-    n = 0
-    while time.perf_counter() - t0 < seconds:
+    for _ in range(reps):
         _cpu_step(d)
-        n += 1
-    dt = (time.perf_counter() - t0) / n
+    dt = (time.perf_counter() - t0) / reps
     return {"value": round(nbytes / dt / 1e9, 2), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"reference.py ops restated on CPU tensors (oracle/ref_torch.py): softmax 1024 rows, "
-                      f"layernorm 4096 rows, rope 1x32 heads (q,k), reduce 2^27; same shapes per row, "
-                      f"sample larger than the last-level cache; "
-                      f"{n} reps in {seconds:.0f}s; {nbytes / 1e9:.3f} GB per rep",
+            "sample": f"{CPU_SAMPLE}; {reps} steps after 1 warm-up, {dt * 1e3:.0f} ms per step, "
+                      f"{nbytes / 1e9:.3f} GB per step",
             "cpu_model": _cpu_model()}
 
 
@@ -492,7 +583,7 @@ def reference_arm(args):
         return
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    d, nbytes = _cpu_sample()
+    d, nbytes = _cpu_inputs()
     for _ in range(args.warmup):
         _cpu_step(d)
     t0 = time.perf_counter()
@@ -505,10 +596,11 @@ def reference_arm(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16 (reduce: fp32)", "data": "synthetic (seeded)",
-        "config": {"workload": "configs[1] memory-bound sweep, bounded CPU sample (rank 0 only)"},
+        "config": {"workload": "configs[1] memory-bound sweep at full size on the host cores "
+                               "(rank 0 only; the same per-GPU workload as the GPU arm's step)",
+                   "global_bytes_per_step": nbytes},
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": "softmax 1024x32768, layernorm 4096x4096, rope q,k 1x32x4096x128, "
-                                   "reduce 2^27 fp32 per step (reference.py ops on CPU tensors)"},
+                         "sample": CPU_SAMPLE},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
@@ -542,7 +634,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--op-reps", type=int, default=20)
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-reps", type=int, default=20, help="timed CPU-baseline steps")
     ap.add_argument("--no-ops", action="store_true", help="skip the GEMM/MLP/attention/CE/RMSNorm lines")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-llama", action="store_true", help="skip the LLaMA-7B forward line")

@@ -64,18 +64,23 @@ AK_API void ak_set_force_simt(int on);
  * kernel instead of the single-CTA one (also AK_GEMM_PAIR=1 at load time).  Same results
  * within rounding order of the accumulator; no reference counterpart (a kernel choice). */
 AK_API void ak_set_gemm_pair(int on);
-/* 1 runs head_dim-128 attention on the CTA-pair (cta_group::2) tcgen05 kernel instead of
- * the single-CTA one (also AK_ATTN_PAIR=1 at load time).  Same results within rounding of
- * the exponentials; no reference counterpart (a kernel choice). */
-AK_API void ak_set_attn_pair(int on);
 
 /* ----------------------------------------------------------------- row ops */
 
-/* y = x / sqrt(mean(x^2, -1) + eps) * w over rows of length `cols`.
+/* y = x / sqrt(mean(x^2, -1) + eps) * w over rows of length `cols`, with reference.py's
+ * rounding: each of x*x, the mean, + eps, sqrt, x / rms and * w is rounded to the input
+ * dtype (the mean's sum accumulates in fp32), so fp16 inputs with |x| > 256 overflow x*x
+ * exactly as the reference does.
  * Replaces kernels/rmsnorm.py:45 kernel_fn(x, weight, eps) and
  * kernels/cuda/rmsnorm.py:171 (reference oracle reference.py:26-29). */
 AK_API int ak_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t cols, int64_t ldx,
                int64_t ldy, float eps, int dtype, void* stream);
+
+/* y = x * rsqrt(mean(x^2, -1) + eps) * w with every intermediate in fp32 and one rounding:
+ * the RMSNorm of models/llama_7b.py:22-30 (RMSNorm.forward) without its 16-bit overflow of
+ * x^2; used by the model path. */
+AK_API int ak_rmsnorm_fp32(const void* x, const void* w, void* y, int64_t rows, int64_t cols,
+                    int64_t ldx, int64_t ldy, float eps, int dtype, void* stream);
 
 /* y = (x - mean) / sqrt(var + eps) * w + b over rows.
  * Replaces kernels/layernorm.py:65 kernel_fn(x, weight, bias, eps)

@@ -69,3 +69,47 @@ def check(y: torch.Tensor, exact, op: str, name: str = "", scale_tol: float = 1.
 
 def to_np(t: torch.Tensor) -> np.ndarray:
     return t.detach().cpu().double().numpy() if t.is_floating_point() else t.detach().cpu().numpy()
+
+
+def check_like_reference(y: torch.Tensor, ref_native: torch.Tensor, exact, op: str,
+                         name: str = "", max_ulps: float = 1.0, abs_floor: float = 0.0) -> None:
+    """For kernels that follow reference.py's own per-operator rounding in 16-bit dtypes
+    (RMSNorm, RoPE with tables in x's dtype, the SwiGLU hidden): y must be within `max_ulps`
+    output quanta of reference.py's output on the same inputs (0: bit-identical) or, where
+    given, within `abs_floor` of it, and within the operator's tolerance of the float64 value
+    once the reference's own rounding error |ref_native - exact| is allowed for."""
+    got = y.detach().float().cpu().double().numpy()
+    r = ref_native.detach().float().double().numpy()
+    assert got.shape == r.shape, f"{name}: shape {got.shape} vs {r.shape}"
+    both_nan = np.isnan(got) & np.isnan(r)
+    d = np.where(both_nan, 0.0, np.abs(got - r))
+    lim = max_ulps * quantum(r, y.dtype) if y.dtype != torch.float32 else 1e-6 * (1 + np.abs(r))
+    lim = np.maximum(lim, abs_floor)
+    bad = ~(d <= lim)
+    assert not bad.any(), (f"{name}: {int(bad.sum())}/{bad.size} elements more than {max_ulps} "
+                           f"ulp from reference.py's output, max diff {np.nanmax(d):.3e}")
+    e = np.asarray(exact, dtype=np.float64)
+    atol, rtol = TOL[OP_CLASS[op]][y.dtype]
+    fin = np.isfinite(e) & np.isfinite(r)
+    bound = atol + rtol * np.abs(e[fin]) + quantum(e[fin], y.dtype) + np.abs(r[fin] - e[fin])
+    err = np.abs(got[fin] - e[fin])
+    assert (err <= bound).all(), (f"{name}: {int((err > bound).sum())} elements beyond the f64 "
+                                  f"tolerance widened by the reference's own rounding")
+
+
+def reference_mlp_hidden(x, w_gate, w_up, activation: str = "silu", dtype=torch.bfloat16):
+    """reference.py's SwiGLU hidden (reference.py:45-55) on float64 projections: the gate and
+    up projections stored in `dtype`, the activation applied to the stored gate and stored, the
+    product stored -- the rounding points of the reference's own 16-bit path, without the
+    rounding noise of any particular GEMM.  Returns a CPU tensor of `dtype`."""
+    import torch.nn.functional as F
+    xf = np.asarray(to_np(x) if isinstance(x, torch.Tensor) else x, dtype=np.float64)
+    g = torch.from_numpy(xf @ to_np(w_gate).T).to(dtype)
+    u = torch.from_numpy(xf @ to_np(w_up).T).to(dtype)
+    if activation == "silu":
+        g = F.silu(g)
+    elif activation == "gelu":
+        g = F.gelu(g)
+    elif activation == "relu2":
+        g = F.relu(g) ** 2
+    return g * u

@@ -4,18 +4,24 @@ Each case calls one operator twice on seeded inputs (the first call warms the ke
 the second is the one to capture: ``ncu -k regex:<kernel> -s 1 -c 1``), keeps the device
 footprint to a few GB and exits non-zero if the device status word reports a timeout.
 
-    python -m autokernel_b200.profile_cases attn      # attn_kernel: causal 2x32x4096x128 bf16
-    python -m autokernel_b200.profile_cases gemm_mn   # gemm_kernel: 4096^3 bf16, B row-major
-    python -m autokernel_b200.profile_cases gemm_k    # gemm_kernel: x[16384,4096] @ W[11008,4096]^T
+    python tests/profile_cases.py attn        # attn_kernel: causal 2x32x4096x128 bf16
+    python tests/profile_cases.py gemm_mn     # gemm_kernel: 4096^3 bf16, B row-major
+    python tests/profile_cases.py gemm_k      # gemm_kernel: x[16384,4096] @ W[11008,4096]^T
+    python tests/profile_cases.py layernorm   # row_reg_kernel: LayerNorm 16384x4096 bf16 (full size)
+
+These are the workloads behind the summaries in profiles/; they are test-side recipes, not
+part of the library.
 """
 from __future__ import annotations
 
 import argparse
 import sys
+from pathlib import Path
 
 import torch
 
-from . import _lib, ops
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+from autokernel_b200 import _lib, ops  # noqa: E402
 
 
 def _attn():
@@ -39,7 +45,15 @@ def _gemm_k():
     return lambda: ops.linear(x, w)
 
 
-CASES = {"attn": _attn, "gemm_mn": _gemm_mn, "gemm_k": _gemm_k}
+def _layernorm():
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(16384, 4096, device="cuda", generator=g, dtype=torch.bfloat16)
+    w = 1 + 0.1 * torch.randn(4096, device="cuda", generator=g, dtype=torch.bfloat16)
+    b = 0.1 * torch.randn(4096, device="cuda", generator=g, dtype=torch.bfloat16)
+    return lambda: ops.layernorm(x, w, b)
+
+
+CASES = {"attn": _attn, "gemm_mn": _gemm_mn, "gemm_k": _gemm_k, "layernorm": _layernorm}
 
 
 def main(argv=None) -> int:

@@ -1,0 +1,173 @@
+"""GPU parity at the sizes the benchmarks run: the persistent tensor-core GEMM past the first
+tile of every CTA, and every BASELINE contraction shape at full size.
+
+The tcgen05 GEMM runs one CTA per SM and walks tiles t, t + 148, ...; its second and later
+tiles use the other TMEM accumulator buffer, flipped barrier phases and a shared-memory ring
+that wraps across tile boundaries.  The cases here give every CTA at least three tiles and are
+compared with the float64 oracle on every row (mid-size cases) or on one seeded row of every
+128-row tile (full BASELINE sizes, where `A[rows] @ B` is the same arithmetic as
+`(A @ B)[rows]`).  Attention at [8, 32, 4096, 128] is compared on sampled (batch, head) pairs.
+Inputs are drawn on the GPU from seeded generators with the BASELINE distributions.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ref_f64
+from parity import check, check_like_reference, reference_mlp_hidden, to_np
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+DTS = {"f16": torch.float16, "bf16": torch.bfloat16}
+TILE_M = 128
+
+
+def ops():
+    from autokernel_b200 import ops as _ops
+    return _ops
+
+
+def lib():
+    from autokernel_b200 import _lib
+    return _lib.load()
+
+
+def _randn(shape, seed, scale=1.0, dtype=torch.bfloat16):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, device=DEV, generator=g) * scale).to(dtype)
+
+
+def sample_rows(M: int, seed: int = 0) -> np.ndarray:
+    """One row per 128-row tile, at a seeded lane that varies from tile to tile (so all four
+    epilogue warps and all 32 lanes are hit), plus the last row."""
+    rng = np.random.default_rng(seed)
+    tiles = (M + TILE_M - 1) // TILE_M
+    rows = np.minimum(np.arange(tiles) * TILE_M + rng.integers(0, TILE_M, tiles), M - 1)
+    return np.unique(np.append(rows, M - 1))
+
+
+def _pair(on: bool):
+    lib().ak_set_gemm_pair(1 if on else 0)
+
+
+# ---------------------------------------------------------------- multi-tile, every row checked
+
+@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 256), (4000, 4000, 200), (2048, 11008, 256)])
+def test_gemm_persistent_multi_tile(dt, M, N, K, pair):
+    """>= 3 tiles per CTA in both B layouts (A @ B with B [K, N]; x @ W^T via W.t()); the
+    (4000, 4000) case ends with partial tiles in the last wave."""
+    A = _randn((M, K), M + K, 1 / math.sqrt(K), DTS[dt])
+    B = _randn((K, N), N + K, 1.0, DTS[dt])
+    W = _randn((N, K), N * 3 + K, 1.0, DTS[dt])
+    _pair(pair)
+    try:
+        y_mn = ops().matmul(A, B)
+        y_k = ops().matmul(A, W.t())
+        torch.cuda.synchronize()
+    finally:
+        _pair(False)
+    a = to_np(A)
+    check(y_mn, ref_f64.matmul(a, to_np(B)), "matmul", f"MN {M}x{N}x{K} pair={pair}")
+    check(y_k, ref_f64.matmul(a, to_np(W).T), "matmul", f"K {M}x{N}x{K} pair={pair}")
+
+
+@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_fused_mlp_multi_tile(dt, pair):
+    """Dual-B gate/up GEMM with 32 x 43 = 1376 tiles (>= 9 per CTA) and the down GEMM."""
+    M, D, H = 4096, 512, 11008
+    x = _randn((M, D), 1, 1.0, DTS[dt])
+    wg, wu = _randn((H, D), 2, 0.02, DTS[dt]), _randn((H, D), 3, 0.02, DTS[dt])
+    wd = _randn((D, H), 4, 0.02, DTS[dt])
+    _pair(pair)
+    try:
+        y = ops().fused_mlp(x, wg, wu, wd)
+        torch.cuda.synchronize()
+    finally:
+        _pair(False)
+    check(y, ref_f64.fused_mlp(to_np(x), to_np(wg), to_np(wu), to_np(wd)), "fused_mlp",
+          f"4096x512x11008 pair={pair}")
+
+
+# ---------------------------------------------------------------- BASELINE shapes, sampled rows
+
+BASELINE_GEMMS = [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384),
+                  (16384, 4096, 4096), (16384, 11008, 4096), (16384, 4096, 11008)]
+
+
+@pytest.mark.parametrize("M,N,K", BASELINE_GEMMS)
+def test_gemm_baseline_shapes_sampled_rows(M, N, K):
+    """bf16, entries N(0,1)/sqrt(K), A [M, K] @ B [K, N]."""
+    A = _randn((M, K), 10 + M + K, 1 / math.sqrt(K))
+    B = _randn((K, N), 20 + N + K, 1 / math.sqrt(K))
+    y = ops().matmul(A, B)
+    torch.cuda.synchronize()
+    rows = sample_rows(M, M + N)
+    ri = torch.as_tensor(rows, device=DEV)
+    check(y[ri], ref_f64.matmul(to_np(A[ri]), to_np(B)), "matmul", f"{M}x{N}x{K} sampled")
+    del A, B, y
+
+
+@pytest.mark.parametrize("M,N,K", [(16384, 4096, 4096), (16384, 11008, 4096), (16384, 4096, 11008)])
+def test_linear_llama_shapes_sampled_rows(M, N, K):
+    """The LLaMA projections as the model runs them: x @ W^T with W [N, K] (K-major B)."""
+    x = _randn((M, K), 30 + K, 1.0)
+    W = _randn((N, K), 40 + N, 0.02)
+    y = ops().matmul(x, W.t())
+    torch.cuda.synchronize()
+    ri = torch.as_tensor(sample_rows(M, N), device=DEV)
+    check(y[ri], ref_f64.matmul(to_np(x[ri]), to_np(W).T), "matmul", f"linear {M}x{N}x{K}")
+
+
+def test_fused_mlp_baseline_sampled_rows():
+    """BASELINE configs[3] MLP: x [16384, 4096] ~ N(0,1), weights N(0, 0.02), H = 11008.
+
+    At this size the gate reaches |g| ~ 5 and the hidden |h| ~ 20, and the hidden is stored in
+    bf16 between the two GEMMs with reference.py's roundings (gate, up, silu(gate) and the
+    product each rounded to bf16).  A half-ulp of 20 in bf16 is 0.06, and 11008 such roundings
+    summed through weights of 0.02 move single outputs by more than the 1e-2 tolerance from the
+    float64 value (the reference's own bf16 output misses it by more than 1e-2 on ~2% of these
+    elements).  So the check is split at that rounding point: the hidden against reference.py's
+    rounding of the float64 projections, and the output against the float64 down projection of
+    that hidden.  The hidden may differ by up to 4 ulps where an fp32-accumulated gate or up
+    projection rounds to the other neighbour than the exact one (each such flip is 1 ulp of g
+    or u, which silu(g) * u carries into the product, plus the product's own rounding), or by
+    up to 1e-3 where the hidden is that small: for a gate far below zero silu(g) ~ g e^g has a
+    relative sensitivity of ~|g|, so one flipped ulp of g is many ulps of a tiny hidden."""
+    M, D, H = 16384, 4096, 11008
+    x = _randn((M, D), 50)
+    wg, wu, wd = _randn((H, D), 51, 0.02), _randn((H, D), 52, 0.02), _randn((D, H), 53, 0.02)
+    h = ops().mlp_hidden(x, wg, wu)
+    y = ops().fused_mlp(x, wg, wu, wd)
+    torch.cuda.synchronize()
+    ri = torch.as_tensor(sample_rows(M, 5), device=DEV)
+    hr = reference_mlp_hidden(x[ri], wg, wu)
+    check_like_reference(h[ri], hr, ref_f64.mlp_hidden(to_np(x[ri]), to_np(wg), to_np(wu)),
+                         "fused_mlp", "hidden 16384x4096x11008 sampled", max_ulps=4,
+                         abs_floor=1e-3)
+    check(y[ri], to_np(hr) @ to_np(wd).T, "fused_mlp", "16384x4096x11008 sampled")
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_baseline_sampled_heads(causal):
+    """BASELINE configs[3] attention: Q, K, V [8, 32, 4096, 128] ~ N(0,1), scale 1/sqrt(128);
+    four seeded (batch, head) pairs compared with the f64 oracle in full."""
+    B, H, S, D = 8, 32, 4096, 128
+    Q, K, V = (_randn((B, H, S, D), 60 + i) for i in range(3))
+    y = ops().flash_attention(Q, K, V, causal=causal)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(7)
+    pairs = [(0, 0), (B - 1, H - 1)] + [(int(b), int(h)) for b, h in
+                                        zip(rng.integers(0, B, 2), rng.integers(0, H, 2))]
+    for b, h in pairs:
+        e = ref_f64.attention(to_np(Q[b, h]), to_np(K[b, h]), to_np(V[b, h]), causal)
+        check(y[b, h], e, "flash_attention", f"b={b} h={h} causal={causal}")
+    from autokernel_b200 import _lib
+    assert _lib.device_status() == 0
