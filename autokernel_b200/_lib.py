@@ -42,6 +42,9 @@ SIGNATURES = {
     "ak_cross_entropy_rows": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _i64, _vp, _vp, _vp, _vp, _vp]),
     "ak_cross_entropy_finalize": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _i32, _vp]),
     "ak_mean_from_sum_count": (_i32, [_vp, _vp, _i32, _vp]),
+    "ak_linear_cross_entropy_workspace_size": (_sz, [_i64, _i64]),
+    "ak_linear_cross_entropy_rows": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _i64,
+                                            _vp, _sz, _vp, _vp, _vp, _vp, _vp]),
     "ak_matmul": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ak_matmul_add": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ak_linear_rope": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),

@@ -12,6 +12,17 @@ struct RopeEpilogue {
   int T = 1, head_dim = 2, cols = 0;
 };
 
+// LM head + cross entropy (MODE_XENT): per-row partials of every 256-column vocab tile.
+struct XentEpilogue {
+  const int64_t* targets = nullptr;  // [M]
+  float* part = nullptr;             // [ceil(N / 256)][M] pairs (max, sum of exp)
+  float* tgt = nullptr;              // [M] target logits (written by the tile holding them)
+};
+constexpr int kXentTileN = 256;
+
+int tc_gemm_xent(int dtype, const void* x, const void* w, int M, int N, int K, int64_t ldx,
+                 int64_t ldw, const XentEpilogue& xe, cudaStream_t st);
+
 bool tc_gemm_ok(int dtype, const void* A, const void* B, const void* B2, int64_t K, int64_t lda,
                 int64_t ldb, bool b_mn);
 int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, void* C, int M,

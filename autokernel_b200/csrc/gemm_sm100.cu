@@ -5,6 +5,10 @@
 //   MODE_K    B is [N, K] row-major (x @ W^T, the down projection)
 //   MODE_DUAL two K-major weights Wg, Wu [H, K]: the epilogue writes
 //             act(x @ Wg^T) * (x @ Wu^T), the SwiGLU hidden, in one pass.
+//   MODE_XENT B is [N, K] (an LM head [vocab, dim]): nothing is stored; the epilogue
+//             rounds each logit to the dtype and reduces every row of its 256-column vocab
+//             tile to (max, sum of exp(logit - max)), and copies out the target's logit
+//             when the target falls in the tile (cross entropy without the logits tensor).
 //
 // Structure: persistent CTAs (one per SM, 192 threads), warp-specialised:
 //   warp 0      TMA producer: 4-stage ring of {A 128x64, B 256x64} tiles,
@@ -85,7 +89,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;
 constexpr int TMEM_COLS = 512;
 
-enum { MODE_K = 0, MODE_MN = 1, MODE_DUAL = 2 };
+enum { MODE_K = 0, MODE_MN = 1, MODE_DUAL = 2, MODE_XENT = 3 };
 
 struct Params {
   int M, N, K;  // N = output columns (hidden columns in MODE_DUAL)
@@ -102,7 +106,78 @@ struct Params {
   const float* rope_cos;
   const float* rope_sin;
   int rope_T, rope_hd, rope_cols;
+  // MODE_XENT: targets [M] (int64), partials [tiles_n][M] of (max, sum exp), target logits [M]
+  const int64_t* xt_targets;
+  float2* xt_part;
+  float* xt_tgt;
 };
+
+// max of 32 floats with the 3-input max (depth 4)
+AK_D float max32f(const float* v) {
+  float a[11];
+#pragma unroll
+  for (int t = 0; t < 10; ++t) a[t] = fmax3(v[3 * t], v[3 * t + 1], v[3 * t + 2]);
+  a[10] = fmaxf(v[30], v[31]);
+  const float w0 = fmax3(a[0], a[1], a[2]), w1 = fmax3(a[3], a[4], a[5]);
+  const float w2 = fmax3(a[6], a[7], a[8]), w3 = fmaxf(a[9], a[10]);
+  return fmaxf(fmax3(w0, w1, w2), w3);
+}
+
+// Cross-entropy epilogue of one row of a 256-column vocab tile (MODE_XENT).  The logits are
+// rounded to the dtype first -- the values an unfused LM head would store -- so the row max
+// and the target logit are bitwise those of the unfused path (reference.py:58-60 over
+// models/llama_7b.py's logits).
+template <int DT>
+AK_D void xent_row_tile(const Params& p, uint32_t tbase, int row, int tn) {
+  constexpr float kL2e = 1.4426950408889634f;
+  const int64_t tg = row < p.M ? __ldg(p.xt_targets + row) : -1;
+  const int col0 = tn * BN;
+  const int64_t rel = tg - col0;
+  float m = -INFINITY, s = 0.f, tl = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(tbase + c, r);
+    tmem_wait_ld();
+    tmem_regs_ready(r);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      v[j] = __uint_as_float(r[j]);
+      v[j + 1] = __uint_as_float(r[j + 1]);
+      rnd2<DT>(v[j], v[j + 1]);
+    }
+    if (col0 + c + 32 > p.N) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + c + j >= p.N) v[j] = -INFINITY;
+    }
+    const float cm = max32f(v);
+    if (cm > m) {
+      s = (m == -INFINITY) ? 0.f : s * ex2_approx((m - cm) * kL2e);
+      m = cm;
+    }
+    if (m != -INFINITY) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        s0 += ex2_approx((v[j] - m) * kL2e);
+        s1 += ex2_approx((v[j + 1] - m) * kL2e);
+      }
+      s += s0 + s1;
+    }
+    const int64_t rc = rel - c;
+    if (rc >= 0 && rc < 32) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j == rc) tl = v[j];
+    }
+  }
+  if (row < p.M) {
+    p.xt_part[(int64_t)tn * p.M + row] = make_float2(m, s);
+    if (rel >= 0 && rel < BN && col0 + rel < p.N) p.xt_tgt[row] = tl;
+  }
+}
 
 AK_D void tile_coords(int t, const Params& p, int& tm, int& tn) {
   const int group = GROUP_M * p.tiles_n;
@@ -222,7 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_expect_tx(&full[s], STAGE_BYTES);
           const int k0 = kb * BK;
           tma_load_2d(sa, &ta, &full[s], k0, m0);
-          if (MODE == MODE_K) {
+          if (MODE == MODE_K || MODE == MODE_XENT) {
             tma_load_2d(sb, &tb, &full[s], k0, tn * BN);
           } else if (MODE == MODE_DUAL) {
             tma_load_2d(sb, &tb, &full[s], k0, tn * (BN / 2));
@@ -291,7 +366,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       tile_coords(t, p, tm, tn);
       const int row = tm * BM + q * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * BN;
-      if (MODE != MODE_DUAL) {
+      if (MODE == MODE_XENT) {
+        xent_row_tile<DT>(p, tbase, row, tn);
+      } else if (MODE != MODE_DUAL) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
@@ -538,7 +615,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 template <int DT, int MODE>
 static int launch(const void* A, const void* B, const void* B2, void* C, int M, int N, int K,
                   int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R, int64_t ldr,
-                  const RopeEpilogue& rope, cudaStream_t st) {
+                  const RopeEpilogue& rope, cudaStream_t st, const XentEpilogue* xent = nullptr) {
   CUtensorMap ta, tb, tb2;
   {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, str[1] = {(uint64_t)lda * 2};
@@ -580,6 +657,9 @@ static int launch(const void* A, const void* B, const void* B2, void* C, int M, 
   p.rope_T = rope.T;
   p.rope_hd = rope.head_dim;
   p.rope_cols = rope.cols;
+  p.xt_targets = xent ? xent->targets : nullptr;
+  p.xt_part = xent ? reinterpret_cast<float2*>(xent->part) : nullptr;
+  p.xt_tgt = xent ? xent->tgt : nullptr;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, BM, BN, false, MODE == MODE_MN);
 
   const cudaError_t attr_err = smem_optin<gemm_kernel<DT, MODE>>(SMEM_BYTES);
@@ -635,6 +715,9 @@ static int launch_pair(const void* A, const void* B, const void* B2, void* C, in
   p.rope_T = rope.T;
   p.rope_hd = rope.head_dim;
   p.rope_cols = rope.cols;
+  p.xt_targets = nullptr;
+  p.xt_part = nullptr;
+  p.xt_tgt = nullptr;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, 256, BN, false, MODE == MODE_MN);
 
   const cudaError_t attr_err = smem_optin<gemm_pair_kernel<DT, MODE>>(P_SMEM_BYTES);
@@ -692,6 +775,16 @@ int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, v
   if (dtype == AK_BF16) { AK_TCG(AK_BF16) }
   AK_TCG(AK_F16)
 #undef AK_TCG
+}
+
+int tc_gemm_xent(int dtype, const void* x, const void* w, int M, int N, int K, int64_t ldx,
+                 int64_t ldw, const XentEpilogue& xe, cudaStream_t st) {
+  using namespace gemm;
+  if (dtype == AK_BF16)
+    return launch<AK_BF16, MODE_XENT>(x, w, nullptr, nullptr, M, N, K, ldx, ldw, 0, 0, nullptr,
+                                      0, RopeEpilogue(), st, &xe);
+  return launch<AK_F16, MODE_XENT>(x, w, nullptr, nullptr, M, N, K, ldx, ldw, 0, 0, nullptr, 0,
+                                   RopeEpilogue(), st, &xe);
 }
 
 }  // namespace ak

@@ -17,7 +17,9 @@ Every arithmetic step is one of this package's kernels:
     attention            ops.attention_bhsd    (reads [B, T, H, D] views, GQA, causal)
     SwiGLU MLP           ops.mlp_hidden + ops.linear (dual GEMM + SiLU*mul epilogue, down GEMM)
     residual adds        in the o-projection / down-projection GEMM epilogues, in place
-    LM head + loss       ops.linear, ops.cross_entropy (ignore_index masks the last position)
+    LM head + loss       ops.linear_cross_entropy_partial: one tcgen05 GEMM whose epilogue
+                         reduces each vocab tile to (max, sum exp) and the target logit
+                         (the logits are never stored; ignore_index masks the last position)
 Glue left to torch: the embedding gather.
 """
 from __future__ import annotations
@@ -143,15 +145,19 @@ class LlamaB200:
         return h
 
     @torch.no_grad()
-    def forward(self, tokens: torch.Tensor) -> torch.Tensor:
-        """Logits [B, T, vocab] (models/llama_7b.py:199-209)."""
+    def hidden(self, tokens: torch.Tensor) -> torch.Tensor:
+        """The final normalised hidden state [B, T, dim], the LM head's input."""
         _, T = tokens.shape
         cos, sin = self._tables(T, tokens.device)
         h = torch.nn.functional.embedding(tokens, self.w["tok_embeddings.weight"])  # new tensor
         for i in range(self.cfg.n_layers):
             h = self._layer(i, h, cos, sin)
-        h = ops.rmsnorm_fp32(h, self.w["norm.weight"], self.cfg.norm_eps)
-        return ops.linear(h, self.w["output.weight"])
+        return ops.rmsnorm_fp32(h, self.w["norm.weight"], self.cfg.norm_eps)
+
+    @torch.no_grad()
+    def forward(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Logits [B, T, vocab] (models/llama_7b.py:199-209)."""
+        return ops.linear(self.hidden(tokens), self.w["output.weight"])
 
     __call__ = forward
 
@@ -166,11 +172,16 @@ class LlamaB200:
     @torch.no_grad()
     def loss(self, tokens: torch.Tensor, group=None) -> torch.Tensor:
         """Mean next-token cross entropy; with a process group, the mean over all ranks'
-        sequences (one fp64 all-reduce of (sum, count))."""
-        logits = self.forward(tokens)
+        sequences (one fp64 all-reduce of (sum, count)).  The LM head and the loss run as one
+        fused kernel (ops.linear_cross_entropy_rows): the [B*T, vocab] logits are never
+        stored."""
+        h = self.hidden(tokens)
         targets = self.next_token_targets(tokens)
-        V = logits.shape[-1]
-        return shard.cross_entropy_sharded(logits.view(-1, V), targets.view(-1), group=group)
+        W = self.w["output.weight"]
+        return shard.cross_entropy_sharded(
+            h.view(-1, h.shape[-1]), targets.view(-1), group=group,
+            partial_fn=lambda x, t: ops.linear_cross_entropy_partial(x, W, t),
+            out_dtype=h.dtype)
 
 
 def model_flops(cfg: LlamaConfig, batch: int, seq_len: int) -> float:

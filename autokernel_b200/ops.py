@@ -274,6 +274,61 @@ def cross_entropy(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def linear_cross_entropy_rows(x: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
+                              with_stats: bool = False):
+    """Per-row cross entropy of the logits x @ weight^T (an LM head [vocab, dim]) without
+    materialising them: (loss fp32 [N], targets int64 [N]) and, with_stats, the row max and
+    target logit, bitwise those of linear() followed by cross_entropy_rows().  16-bit x and
+    weight use the fused tensor-core kernel; other dtypes run linear() and
+    cross_entropy_rows() (this package's kernels, with the logits stored)."""
+    require_cuda(x, weight, targets)
+    x2 = _rows_view(x)
+    n, dim = x2.shape
+    vocab = weight.shape[0]
+    if weight.dim() != 2 or weight.shape[1] != dim or weight.dtype != x.dtype:
+        raise ValueError("linear_cross_entropy: weight must be [vocab, dim] of x's dtype")
+    t = targets.reshape(-1).to(torch.int64).contiguous()
+    if t.numel() != n:
+        raise ValueError(f"targets has {t.numel()} entries for {n} rows")
+    w = weight if weight.stride(1) == 1 else weight.contiguous()
+    fused = (x.dtype in (torch.float16, torch.bfloat16) and x2.stride(1) == 1
+             and x2.stride(0) % 8 == 0 and w.stride(0) % 8 == 0 and dim % 8 == 0
+             and x2.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0)
+    if not fused:
+        return cross_entropy_rows(linear(x2, w), t, with_stats)
+    loss = torch.empty(n, dtype=torch.float32, device=x.device)
+    mx = torch.empty(n, dtype=torch.float32, device=x.device) if with_stats else None
+    tl = torch.empty(n, dtype=torch.float32, device=x.device) if with_stats else None
+    ws = torch.empty(_lib.load().ak_linear_cross_entropy_workspace_size(n, vocab),
+                     dtype=torch.uint8, device=x.device)
+    call("ak_linear_cross_entropy_rows", x2.data_ptr(), w.data_ptr(), t.data_ptr(), n, vocab, dim,
+         x2.stride(0), w.stride(0), dtype_code(x.dtype), IGNORE_INDEX, ws.data_ptr(), ws.numel(),
+         loss.data_ptr(), mx.data_ptr() if mx is not None else None,
+         tl.data_ptr() if tl is not None else None, None, stream_ptr(x.device))
+    return (loss, t, mx, tl) if with_stats else (loss, t)
+
+
+def linear_cross_entropy_partial(x: torch.Tensor, weight: torch.Tensor,
+                                 targets: torch.Tensor) -> torch.Tensor:
+    """fp64 [sum of row losses, counted rows] of the LM head + cross entropy on this shard."""
+    loss, t = linear_cross_entropy_rows(x, weight, targets)
+    sc = torch.empty(2, dtype=torch.float64, device=x.device)
+    call("ak_cross_entropy_finalize", loss.data_ptr(), t.data_ptr(), loss.numel(), IGNORE_INDEX,
+         sc.data_ptr(), None, 0, stream_ptr(x.device))
+    return sc
+
+
+def linear_cross_entropy(x: torch.Tensor, weight: torch.Tensor,
+                         targets: torch.Tensor) -> torch.Tensor:
+    """Mean cross entropy (reference.py:58-60) of the logits x @ weight^T, without storing
+    them; 0-d in x's dtype."""
+    loss, t = linear_cross_entropy_rows(x, weight, targets)
+    out = torch.empty((), dtype=x.dtype, device=x.device)
+    call("ak_cross_entropy_finalize", loss.data_ptr(), t.data_ptr(), loss.numel(), IGNORE_INDEX,
+         None, out.data_ptr(), dtype_code(x.dtype), stream_ptr(x.device))
+    return out
+
+
 # ---------------------------------------------------------------- contractions
 
 def _b_operand(B: torch.Tensor):

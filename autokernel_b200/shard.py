@@ -63,15 +63,19 @@ def reduce_sum_sharded(x_local: torch.Tensor, group=None, out_dtype: torch.dtype
 
 
 def cross_entropy_sharded(logits_local: torch.Tensor, targets_local: torch.Tensor, group=None,
-                          partial_fn: Callable = _default_partial_ce) -> torch.Tensor:
-    """Mean cross entropy over all ranks' rows (rows with target -100 are not counted)."""
+                          partial_fn: Callable = _default_partial_ce,
+                          out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Mean cross entropy over all ranks' rows (rows with target -100 are not counted).
+    `partial_fn(x, targets)` gives the shard's fp64 (sum, count); with a fused LM head x is
+    the hidden state rather than the logits."""
     sc = partial_fn(logits_local, targets_local)
     if dist.is_available() and dist.is_initialized():
         dist.all_reduce(sc, op=dist.ReduceOp.SUM, group=group)
+    dtype = out_dtype or logits_local.dtype
     if sc.is_cuda:
         from . import ops
-        return ops.mean_from_sum_count(sc, logits_local.dtype)
-    return (sc[0] / sc[1]).to(logits_local.dtype)
+        return ops.mean_from_sum_count(sc, dtype)
+    return (sc[0] / sc[1]).to(dtype)
 
 
 def max_over_ranks(value: float, device=None, group=None) -> float:

@@ -154,6 +154,22 @@ AK_API int ak_cross_entropy_finalize(const float* row_loss, const int64_t* targe
 /* *out = sum_count[0] / sum_count[1] in out_dtype (after an all-reduce). */
 AK_API int ak_mean_from_sum_count(const double* sum_count, void* out, int out_dtype, void* stream);
 
+/* LM head fused with cross entropy: row_loss[r] = logsumexp(z_r) - z_r[t_r] for the logits
+ * z = x @ w^T (x [rows, dim], w [vocab, dim] row-major, 16-bit), without storing z.  Each
+ * logit is rounded to the dtype before it enters the loss, so row_max / row_target_logit
+ * (optional) are bitwise those of ak_matmul followed by ak_cross_entropy_rows.  Rows with
+ * t_r == ignore_index get loss 0; other targets outside [0, vocab) give NaN and set
+ * *bad_target.  workspace: ak_linear_cross_entropy_workspace_size(rows, vocab) bytes
+ * (per-row partials of each 256-column vocab tile).  Finish with ak_cross_entropy_finalize.
+ * Replaces the output projection + loss of models/llama_7b.py:199-209 as evaluated by
+ * reference.py:58-60 (cross_entropy_ref over the LM head's logits). */
+AK_API size_t ak_linear_cross_entropy_workspace_size(int64_t rows, int64_t vocab);
+AK_API int ak_linear_cross_entropy_rows(const void* x, const void* w, const int64_t* targets,
+                                 int64_t rows, int64_t vocab, int64_t dim, int64_t ldx,
+                                 int64_t ldw, int dtype, int64_t ignore_index, void* workspace,
+                                 size_t ws_bytes, float* row_loss, float* row_max,
+                                 float* row_target_logit, int* bad_target, void* stream);
+
 /* ----------------------------------------------------------------- contractions */
 
 /* C[M, N] = A[M, K] @ B where B is [K, N] row-major (b_kmajor = 0) or the
