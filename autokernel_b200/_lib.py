@@ -48,6 +48,11 @@ SIGNATURES = {
     "ak_matmul": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ak_matmul_add": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ak_linear_rope": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
+    "ak_row_sumsq": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _vp]),
+    "ak_linear_rms": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i32, _f32,
+                             _vp, _i32, _vp]),
+    "ak_mlp_gate_up_rms": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i32, _f32, _i32, _i32,
+                                  _vp]),
     "ak_mlp_gate_up": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ak_fused_mlp": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ak_flash_attention": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _vp]),

@@ -174,3 +174,101 @@ extern "C" int ak_flash_attention(const void* Q, const void* K, const void* V, v
   return simt_attention_any(dtype, Q, K, V, O, batch_heads, (int)Sq, (int)Sk, (int)D, causal,
                             sm_scale, st);
 }
+
+// ------------------------------------------------------------------ RMSNorm folded into GEMMs
+namespace ak {
+// Per-row sums of squares of x [rows, cols] over 256-column tiles: ss[t][row].  One warp per
+// (row, tile); the values are read as 16-byte vectors when the row allows it.
+template <int DT>
+__global__ void __launch_bounds__(256) row_sumsq_kernel(const void* xv, int64_t rows,
+                                                        int64_t cols, int64_t ld, float* ss) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  const int64_t row = (int64_t)blockIdx.y * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t c0 = (int64_t)blockIdx.x * kRmsTileN;
+  const T* x = reinterpret_cast<const T*>(xv) + row * ld;
+  float acc = 0.f;
+  const bool vec = (ld % 8 == 0) && aligned16(xv) && c0 + kRmsTileN <= cols;
+  if (vec) {
+    float f[8];
+    load_vec<DT>(x + c0 + lane * 8, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc = fmaf(f[j], f[j], acc);
+  } else {
+    for (int64_t c = c0 + lane; c < min(c0 + kRmsTileN, cols); c += 32) {
+      const float f = E::to_f(x[c]);
+      acc = fmaf(f, f, acc);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) ss[(int64_t)blockIdx.x * rows + row] = acc;
+}
+}  // namespace ak
+
+extern "C" int ak_row_sumsq(const void* x, int64_t rows, int64_t cols, int64_t ld, int dtype,
+                            float* ss_out, void* stream) {
+  AK_REQUIRE(dtype == AK_F16 || dtype == AK_BF16, AK_ERR_DTYPE, "row_sumsq: 16-bit x only");
+  AK_REQUIRE(rows >= 0 && cols > 0 && ld >= cols && rows < (1LL << 31), AK_ERR_SHAPE,
+             "bad shape");
+  if (rows == 0) return AK_OK;
+  AK_REQUIRE(x && ss_out, AK_ERR_ARG, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  dim3 grid((unsigned)((cols + kRmsTileN - 1) / kRmsTileN), (unsigned)((rows + 7) / 8));
+  if (dtype == AK_BF16)
+    row_sumsq_kernel<AK_BF16><<<grid, 256, 0, st>>>(x, rows, cols, ld, ss_out);
+  else
+    row_sumsq_kernel<AK_F16><<<grid, 256, 0, st>>>(x, rows, cols, ld, ss_out);
+  return launch_status("row_sumsq");
+}
+
+static int rms_common_checks(const void* x, const void* w, int64_t M, int64_t N, int64_t K,
+                             int64_t ldx, int dtype, const float* rs_in, int rs_tiles) {
+  AK_REQUIRE(dtype == AK_F16 || dtype == AK_BF16, AK_ERR_DTYPE,
+             "RMSNorm-fused GEMM: 16-bit operands only (dtype %d)", dtype);
+  AK_REQUIRE(M >= 0 && N > 0 && K > 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31),
+             AK_ERR_SHAPE, "bad shape");
+  AK_REQUIRE(ldx >= K, AK_ERR_SHAPE, "leading dimension too small");
+  AK_REQUIRE(!rs_in || rs_tiles > 0, AK_ERR_ARG, "rs_in given without rs_tiles");
+  AK_REQUIRE(!g_force_simt && tc_gemm_ok(dtype, x, w, nullptr, K, ldx, K, false), AK_ERR_ARG,
+             "RMSNorm-fused GEMM needs the tensor-core path (16-byte aligned operands)");
+  return AK_OK;
+}
+
+extern "C" int ak_linear_rms(const void* x, const void* w, void* C, const void* R, int64_t M,
+                             int64_t N, int64_t K, int64_t ldx, int64_t ldc, int64_t ldr,
+                             const float* rs_in, int rs_tiles, float eps, float* ss_out,
+                             int dtype, void* stream) {
+  int rc = rms_common_checks(x, w, M, N, K, ldx, dtype, rs_in, rs_tiles);
+  if (rc) return rc;
+  AK_REQUIRE(ldc >= N && (!R || ldr >= N), AK_ERR_SHAPE, "leading dimension too small");
+  if (M == 0) return AK_OK;
+  AK_REQUIRE(C, AK_ERR_ARG, "null output");
+  RmsEpilogue rms;
+  rms.rs_in = rs_in;
+  rms.rs_tiles = rs_tiles;
+  rms.eps = eps;
+  rms.ss_out = ss_out;
+  return tc_gemm_rms(dtype, false, x, w, nullptr, C, (int)M, (int)N, (int)K, ldx, K, ldc, 0, R,
+                     ldr, rms, (cudaStream_t)stream);
+}
+
+extern "C" int ak_mlp_gate_up_rms(const void* x, const void* w_gate, const void* w_up,
+                                  void* hidden, int64_t M, int64_t D, int64_t H,
+                                  const float* rs_in, int rs_tiles, float eps, int activation,
+                                  int dtype, void* stream) {
+  int rc = rms_common_checks(x, w_gate, M, H, D, D, dtype, rs_in, rs_tiles);
+  if (rc) return rc;
+  AK_REQUIRE(activation >= AK_ACT_SILU && activation <= AK_ACT_RELU2, AK_ERR_ARG,
+             "unknown activation %d", activation);
+  AK_REQUIRE(aligned16(w_up), AK_ERR_ARG, "w_up not 16-byte aligned");
+  if (M == 0) return AK_OK;
+  AK_REQUIRE(hidden, AK_ERR_ARG, "null output");
+  RmsEpilogue rms;
+  rms.rs_in = rs_in;
+  rms.rs_tiles = rs_tiles;
+  rms.eps = eps;
+  return tc_gemm_rms(dtype, true, x, w_gate, w_up, hidden, (int)M, (int)H, (int)D, D, D, H,
+                     activation, nullptr, 0, rms, (cudaStream_t)stream);
+}

@@ -20,6 +20,22 @@ struct XentEpilogue {
 };
 constexpr int kXentTileN = 256;
 
+// RMSNorm folded into a K-major GEMM: each output row is scaled by 1 / sqrt(mean + eps) from
+// the per-row partial sums of squares rs_in [rs_tiles][M] of the A operand (the norm weight is
+// folded into B), and / or the stored outputs' per-row sums of squares are written to
+// ss_out [ceil(N / 256)][M] for the next norm.
+struct RmsEpilogue {
+  const float* rs_in = nullptr;
+  int rs_tiles = 0;
+  float eps = 0.f;
+  float* ss_out = nullptr;
+};
+constexpr int kRmsTileN = 256;
+
+int tc_gemm_rms(int dtype, bool dual, const void* A, const void* B, const void* B2, void* C,
+                int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act,
+                const void* R, int64_t ldr, const RmsEpilogue& rms, cudaStream_t st);
+
 int tc_gemm_xent(int dtype, const void* x, const void* w, int M, int N, int K, int64_t ldx,
                  int64_t ldw, const XentEpilogue& xe, cudaStream_t st);
 

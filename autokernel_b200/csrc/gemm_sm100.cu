@@ -110,7 +110,24 @@ struct Params {
   const int64_t* xt_targets;
   float2* xt_part;
   float* xt_tgt;
+  // RMSNorm folded into the GEMM (models/llama_7b.py:22-30 in front of a projection):
+  // rs_in [rs_tiles][M] holds per-row sums of squares of A's rows, and each output row is
+  // scaled by 1 / sqrt(sum / K + eps) before rounding (the norm weight is folded into B).
+  // ss_out [tiles_n][M] receives per-row sums of squares of the stored outputs, one per
+  // 256-column tile, for the RMSNorm that follows.
+  const float* rs_in;
+  int rs_tiles;
+  float rs_inv_k, rs_eps;
+  float* ss_out;
 };
+
+// 1 / rms of row `row` from its partial sums of squares
+AK_D float row_scale(const Params& p, int row) {
+  if (!p.rs_in || row >= p.M) return 1.f;
+  float ss = 0.f;
+  for (int t = 0; t < p.rs_tiles; ++t) ss += __ldg(p.rs_in + (int64_t)t * p.M + row);
+  return rsqrtf(ss * p.rs_inv_k + p.rs_eps);
+}
 
 // max of 32 floats with the 3-input max (depth 4)
 AK_D float max32f(const float* v) {
@@ -210,10 +227,11 @@ AK_D void rope_row32(const Params& p, int row, int col, float* v) {
 }
 
 template <int DT>
-AK_D void store_row32(const Params& p, int row, int col, const float* v) {
+AK_D float store_row32(const Params& p, int row, int col, const float* v) {
   using E = Elem<DT>;
   using T = typename E::T;
-  if (row >= p.M) return;
+  float ss = 0.f;
+  if (row >= p.M) return ss;
   T* c = reinterpret_cast<T*>(p.C) + (int64_t)row * p.ldc + col;
   const T* rr = p.R ? reinterpret_cast<const T*>(p.R) + (int64_t)row * p.ldr + col : nullptr;
   if (p.vec_store && col + 32 <= p.N) {
@@ -229,13 +247,21 @@ AK_D void store_row32(const Params& p, int row, int col, const float* v) {
       uint4 raw;
       T* e = reinterpret_cast<T*>(&raw);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) e[j] = E::from_f(v[q * 8 + j] + add[j]);
+      for (int j = 0; j < 8; ++j) {
+        e[j] = E::from_f(v[q * 8 + j] + add[j]);
+        const float st = E::to_f(e[j]);
+        ss = fmaf(st, st, ss);
+      }
       reinterpret_cast<uint4*>(c)[q] = raw;
     }
   } else {
-    for (int j = 0; j < 32 && col + j < p.N; ++j)
-      c[j] = E::from_f(v[j] + (rr ? E::to_f(rr[j]) : 0.f));
+    for (int j = 0; j < 32 && col + j < p.N; ++j) {
+      const T e = E::from_f(v[j] + (rr ? E::to_f(rr[j]) : 0.f));
+      c[j] = e;
+      ss = fmaf(E::to_f(e), E::to_f(e), ss);
+    }
   }
+  return ss;
 }
 
 template <int DT, int MODE>
@@ -366,9 +392,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       tile_coords(t, p, tm, tn);
       const int row = tm * BM + q * 32 + lane;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * BN;
+      const float rsc = row_scale(p, row);
       if (MODE == MODE_XENT) {
         xent_row_tile<DT>(p, tbase, row, tn);
       } else if (MODE != MODE_DUAL) {
+        float ss = 0.f;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
@@ -377,10 +405,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_regs_ready(r);
           float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rsc;
           rope_row32(p, row, tn * BN + c, v);
-          store_row32<DT>(p, row, tn * BN + c, v);
+          ss += store_row32<DT>(p, row, tn * BN + c, v);
         }
+        if (p.ss_out && row < p.M) p.ss_out[(int64_t)tn * p.M + row] = ss;
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
@@ -393,7 +422,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            v[j] = swiglu_ref<DT>(p.act, __uint_as_float(g[j]), __uint_as_float(u[j]));
+            v[j] = swiglu_ref<DT>(p.act, __uint_as_float(g[j]) * rsc, __uint_as_float(u[j]) * rsc);
           store_row32<DT>(p, row, tn * (BN / 2) + c, v);
         }
       }
@@ -615,7 +644,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 template <int DT, int MODE>
 static int launch(const void* A, const void* B, const void* B2, void* C, int M, int N, int K,
                   int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R, int64_t ldr,
-                  const RopeEpilogue& rope, cudaStream_t st, const XentEpilogue* xent = nullptr) {
+                  const RopeEpilogue& rope, cudaStream_t st, const XentEpilogue* xent = nullptr,
+                  const RmsEpilogue* rms = nullptr) {
   CUtensorMap ta, tb, tb2;
   {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, str[1] = {(uint64_t)lda * 2};
@@ -660,6 +690,11 @@ static int launch(const void* A, const void* B, const void* B2, void* C, int M, 
   p.xt_targets = xent ? xent->targets : nullptr;
   p.xt_part = xent ? reinterpret_cast<float2*>(xent->part) : nullptr;
   p.xt_tgt = xent ? xent->tgt : nullptr;
+  p.rs_in = rms ? rms->rs_in : nullptr;
+  p.rs_tiles = rms ? rms->rs_tiles : 0;
+  p.rs_inv_k = 1.f / (float)K;
+  p.rs_eps = rms ? rms->eps : 0.f;
+  p.ss_out = rms ? rms->ss_out : nullptr;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, BM, BN, false, MODE == MODE_MN);
 
   const cudaError_t attr_err = smem_optin<gemm_kernel<DT, MODE>>(SMEM_BYTES);
@@ -718,6 +753,11 @@ static int launch_pair(const void* A, const void* B, const void* B2, void* C, in
   p.xt_targets = nullptr;
   p.xt_part = nullptr;
   p.xt_tgt = nullptr;
+  p.rs_in = nullptr;
+  p.rs_tiles = 0;
+  p.rs_inv_k = 1.f;
+  p.rs_eps = 0.f;
+  p.ss_out = nullptr;
   p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, 256, BN, false, MODE == MODE_MN);
 
   const cudaError_t attr_err = smem_optin<gemm_pair_kernel<DT, MODE>>(P_SMEM_BYTES);
@@ -775,6 +815,25 @@ int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, v
   if (dtype == AK_BF16) { AK_TCG(AK_BF16) }
   AK_TCG(AK_F16)
 #undef AK_TCG
+}
+
+int tc_gemm_rms(int dtype, bool dual, const void* A, const void* B, const void* B2, void* C,
+                int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act,
+                const void* R, int64_t ldr, const RmsEpilogue& rms, cudaStream_t st) {
+  using namespace gemm;
+  const RopeEpilogue none;
+  if (dtype == AK_BF16) {
+    if (dual)
+      return launch<AK_BF16, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, none,
+                                        st, nullptr, &rms);
+    return launch<AK_BF16, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, none, st,
+                                   nullptr, &rms);
+  }
+  if (dual)
+    return launch<AK_F16, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, none, st,
+                                     nullptr, &rms);
+  return launch<AK_F16, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, none, st,
+                                nullptr, &rms);
 }
 
 int tc_gemm_xent(int dtype, const void* x, const void* w, int M, int N, int K, int64_t ldx,

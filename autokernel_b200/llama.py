@@ -11,7 +11,12 @@ module surgery (verify.py:510-641), extended to attention, RoPE, the MLP and the
 loss.
 
 Every arithmetic step is one of this package's kernels:
-    RMSNorm              ops.rmsnorm_fp32      (csrc/rowops.cu, fp32 intermediates)
+    RMSNorm              folded into the projections that read it (16-bit weights): the
+                         o-/down-projection epilogues write per-row sums of squares of the
+                         new hidden state, the q/k/v and gate/up GEMMs scale their rows by
+                         1 / rms with the norm weight folded into their weights, so the
+                         normalised activations are never stored (ops.linear_rms,
+                         ops.mlp_hidden_rms); otherwise ops.rmsnorm_fp32 (csrc/rowops.cu)
     q/k/v/o projections  ops.linear            (tcgen05 GEMM, K-major weights, no copies)
     RoPE                 ops.rope_apply        (fp32 cos/sin table, [B, T, H, D] in place)
     attention            ops.attention_bhsd    (reads [B, T, H, D] views, GQA, causal)
@@ -73,10 +78,15 @@ def rope_tables(seq_len: int, head_dim: int, theta: float, device):
 class LlamaB200:
     """Inference-mode LLaMA whose forward runs on the autokernel_b200 kernels."""
 
-    def __init__(self, cfg: LlamaConfig, weights: dict[str, torch.Tensor]):
+    def __init__(self, cfg: LlamaConfig, weights: dict[str, torch.Tensor],
+                 fuse_norms: bool | None = None):
         self.cfg = cfg
         self.w = weights
         self._rope: dict = {}
+        dt = weights["tok_embeddings.weight"].dtype
+        # RMSNorm folded into the projections after it (16-bit weights: tensor-core GEMMs)
+        self.fuse_norms = dt in (torch.float16, torch.bfloat16) if fuse_norms is None else fuse_norms
+        self._folded: dict[int, tuple] = {}
 
     @staticmethod
     def random_weights(cfg: LlamaConfig, device, dtype=torch.float16, seed: int = 0,
@@ -128,7 +138,32 @@ class LlamaB200:
         v = ops.linear(x, w[p + "attention.wv.weight"]).view(B, T, c.n_kv_heads, hd)
         q = ops.rope_apply(q, cos, sin)
         k = ops.rope_apply(k, cos, sin)
-        o = torch.empty(B, T, c.n_heads, hd, dtype=h.dtype, device=h.device)
+        o = self._attention(q, k, v, B, T)
+        # residual adds happen in the GEMM epilogues, in place on h
+        ops.linear(o.view(B, T, c.n_heads * hd), w[p + "attention.wo.weight"], residual=h, out=h)
+        x = ops.rmsnorm_fp32(h, w[p + "ffn_norm.weight"], c.norm_eps)
+        hidden = ops.mlp_hidden(x, w[p + "feed_forward.w1.weight"], w[p + "feed_forward.w3.weight"])
+        ops.linear(hidden, w[p + "feed_forward.w2.weight"], residual=h, out=h)
+        return h
+
+    def _fold(self, i: int) -> tuple:
+        """Projection weights of layer i with the RMSNorm weight that precedes them folded in
+        (w * diag(norm.weight), rounded once): q, k, v after attention_norm, w1, w3 after
+        ffn_norm.  Built once; the reference weights are kept for the unfused path."""
+        if i not in self._folded:
+            w, p = self.w, f"layers.{i}."
+            an, fn = w[p + "attention_norm.weight"], w[p + "ffn_norm.weight"]
+            self._folded[i] = tuple(
+                ops.fold_norm_weight(w[p + k], n) for k, n in (
+                    ("attention.wq.weight", an), ("attention.wk.weight", an),
+                    ("attention.wv.weight", an), ("feed_forward.w1.weight", fn),
+                    ("feed_forward.w3.weight", fn)))
+        return self._folded[i]
+
+    def _attention(self, q, k, v, B, T):
+        c = self.cfg
+        hd = c.head_dim
+        o = torch.empty(B, T, c.n_heads, hd, dtype=q.dtype, device=q.device)
         r = ops.attention_bhsd(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                causal=True, out=o.transpose(1, 2))
         if r is None:  # layouts / head sizes the tensor-core path cannot take
@@ -137,12 +172,29 @@ class LlamaB200:
                                     k.transpose(1, 2).repeat_interleave(rep, 1),
                                     v.transpose(1, 2).repeat_interleave(rep, 1))
             o = o.transpose(1, 2).contiguous()
-        # residual adds happen in the GEMM epilogues, in place on h
-        ops.linear(o.view(B, T, c.n_heads * hd), w[p + "attention.wo.weight"], residual=h, out=h)
-        x = ops.rmsnorm_fp32(h, w[p + "ffn_norm.weight"], c.norm_eps)
-        hidden = ops.mlp_hidden(x, w[p + "feed_forward.w1.weight"], w[p + "feed_forward.w3.weight"])
-        ops.linear(hidden, w[p + "feed_forward.w2.weight"], residual=h, out=h)
-        return h
+        return o
+
+    def _layer_fused(self, i: int, h: torch.Tensor, ss: torch.Tensor, cos, sin):
+        """One decoder layer with both RMSNorms folded into the GEMMs that read them: ss holds
+        the per-row partial sums of squares of h, and the o-projection and down-projection
+        epilogues (which add the residual into h in place) write those of the new h."""
+        c, w = self.cfg, self.w
+        p = f"layers.{i}."
+        B, T, _ = h.shape
+        hd, eps = c.head_dim, c.norm_eps
+        wq, wk, wv, w1, w3 = self._fold(i)
+        q = ops.linear_rms(h, wq, ss, eps).view(B, T, c.n_heads, hd)
+        k = ops.linear_rms(h, wk, ss, eps).view(B, T, c.n_kv_heads, hd)
+        v = ops.linear_rms(h, wv, ss, eps).view(B, T, c.n_kv_heads, hd)
+        q = ops.rope_apply(q, cos, sin)
+        k = ops.rope_apply(k, cos, sin)
+        o = self._attention(q, k, v, B, T)
+        _, ss = ops.linear_rms(o.view(B, T, c.n_heads * hd), w[p + "attention.wo.weight"],
+                               residual=h, out=h, want_ss=True)
+        hidden = ops.mlp_hidden_rms(h, w1, w3, ss, eps)
+        _, ss = ops.linear_rms(hidden, w[p + "feed_forward.w2.weight"], residual=h, out=h,
+                               want_ss=True)
+        return h, ss
 
     @torch.no_grad()
     def hidden(self, tokens: torch.Tensor) -> torch.Tensor:
@@ -150,8 +202,13 @@ class LlamaB200:
         _, T = tokens.shape
         cos, sin = self._tables(T, tokens.device)
         h = torch.nn.functional.embedding(tokens, self.w["tok_embeddings.weight"])  # new tensor
-        for i in range(self.cfg.n_layers):
-            h = self._layer(i, h, cos, sin)
+        if self.fuse_norms:
+            ss = ops.row_sumsq(h)
+            for i in range(self.cfg.n_layers):
+                h, ss = self._layer_fused(i, h, ss, cos, sin)
+        else:
+            for i in range(self.cfg.n_layers):
+                h = self._layer(i, h, cos, sin)
         return ops.rmsnorm_fp32(h, self.w["norm.weight"], self.cfg.norm_eps)
 
     @torch.no_grad()

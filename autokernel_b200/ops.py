@@ -392,6 +392,70 @@ def linear(x: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor | None 
     return o
 
 
+RMS_TILE = 256  # columns per partial sum of squares
+
+
+def row_sumsq(x: torch.Tensor) -> torch.Tensor:
+    """Per-row sums of squares of x [..., cols] over 256-column tiles: fp32
+    [ceil(cols / 256), rows], the input of the RMSNorm-folded GEMMs."""
+    require_cuda(x)
+    x2 = _rows_view(x)
+    rows, cols = x2.shape
+    ss = torch.empty((cols + RMS_TILE - 1) // RMS_TILE, rows, dtype=torch.float32, device=x.device)
+    call("ak_row_sumsq", x2.data_ptr(), rows, cols, x2.stride(0), dtype_code(x.dtype),
+         ss.data_ptr(), stream_ptr(x.device))
+    return ss
+
+
+def fold_norm_weight(weight: torch.Tensor, norm_weight: torch.Tensor) -> torch.Tensor:
+    """w * diag(norm_weight) for an nn.Linear weight [N, K] read after an RMSNorm over K:
+    the weight the RMSNorm-folded GEMMs multiply by (rounded once to the weight's dtype)."""
+    return (weight.float() * norm_weight.float()[None, :]).to(weight.dtype).contiguous()
+
+
+def linear_rms(x: torch.Tensor, weight: torch.Tensor, rs: torch.Tensor | None = None,
+               eps: float = 1e-6, residual: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, want_ss: bool = False):
+    """x @ weight^T with the rows scaled by 1 / sqrt(mean(x^2) + eps) from rs (the
+    row_sumsq partials of x) -- RMSNorm(x) @ w^T when weight = fold_norm_weight(w, norm
+    weight) -- plus an optional residual added in the epilogue (out may alias it).  With
+    want_ss also returns the partial sums of squares of the result, for the next norm."""
+    require_cuda(x, weight)
+    x2 = _rows_view(x)
+    M, K = x2.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K or weight.dtype != x.dtype or not weight.is_contiguous():
+        raise ValueError("linear_rms: weight must be a contiguous [N, K] of x's dtype")
+    shape = (*x.shape[:-1], N)
+    o = torch.empty(shape, dtype=x.dtype, device=x.device) if out is None else out
+    ss = (torch.empty((N + RMS_TILE - 1) // RMS_TILE, M, dtype=torch.float32, device=x.device)
+          if want_ss else None)
+    r = residual
+    call("ak_linear_rms", x2.data_ptr(), weight.data_ptr(), o.data_ptr(),
+         r.data_ptr() if r is not None else None, M, N, K, x2.stride(0), N, N,
+         rs.data_ptr() if rs is not None else None, rs.shape[0] if rs is not None else 0,
+         float(eps), ss.data_ptr() if ss is not None else None, dtype_code(x.dtype),
+         stream_ptr(x.device))
+    return (o, ss) if want_ss else o
+
+
+def mlp_hidden_rms(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+                   rs: torch.Tensor, eps: float = 1e-6, activation: str = "silu") -> torch.Tensor:
+    """act(g) * u of the row-scaled projections g = RMSNorm(x) @ w_gate^T, u = ... @ w_up^T,
+    with the norm weight folded into w_gate and w_up (fold_norm_weight)."""
+    require_cuda(x, w_gate, w_up, rs)
+    x2 = _rows_view(x)
+    M, D = x2.shape
+    H = w_gate.shape[0]
+    if x2.stride(0) != D:
+        raise ValueError("mlp_hidden_rms: x rows must be contiguous")
+    hidden = torch.empty((*x.shape[:-1], H), dtype=x.dtype, device=x.device)
+    call("ak_mlp_gate_up_rms", x2.data_ptr(), w_gate.data_ptr(), w_up.data_ptr(), hidden.data_ptr(),
+         M, D, H, rs.data_ptr(), rs.shape[0], float(eps), _lib.AK_ACT[activation],
+         dtype_code(x.dtype), stream_ptr(x.device))
+    return hidden
+
+
 def linear_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                 seq_len: int, head_dim: int, rope_cols: int) -> torch.Tensor:
     """x @ weight^T with interleaved RoPE applied in the GEMM epilogue to the first rope_cols

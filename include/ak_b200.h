@@ -203,6 +203,32 @@ AK_API int ak_linear_rope(const void* x, const void* w, void* out, int64_t M, in
 AK_API int ak_mlp_gate_up(const void* x, const void* w_gate, const void* w_up, void* hidden, int64_t M,
                    int64_t D, int64_t H, int activation, int dtype, void* stream);
 
+/* RMSNorm folded into the projections that read it (models/llama_7b.py:22-30 in front of
+ * the q/k/v projections and the feed-forward): with the norm weight folded into the
+ * projection weight (w' = w * diag(norm.weight)), RMSNorm(x) @ w^T equals (x @ w'^T) scaled
+ * per row by 1 / sqrt(mean(x^2) + eps), so the normalised activations are never stored.  The
+ * per-row mean comes from partial sums of squares ss[t][row] over 256-column tiles of x,
+ * written by ak_row_sumsq or by the ss_out of the GEMM that produced x.
+ *   ak_row_sumsq:        ss_out [ceil(cols / 256)][rows] for x [rows, cols] (16-bit).
+ *   ak_linear_rms:       C = rowscale * (x @ w^T) [+ R] with x [M, K], w [N, K]; rs_in
+ *                        (optional) the rs_tiles partials of x; ss_out (optional) receives
+ *                        the partials [ceil(N / 256)][M] of the stored C (after + R), for the
+ *                        next norm.  R may alias C (in-place residual update).
+ *   ak_mlp_gate_up_rms:  hidden = act(g) * u with g, u the row-scaled x @ w_gate^T,
+ *                        x @ w_up^T (reference.py:45-55 rounding of the hidden).
+ * 16-bit operands on the tensor-core path only (AK_ERR_ARG otherwise).  Fused neighbours of
+ * the path: no single reference function; their parts are reference.py:26-29 / :10-12 /
+ * :45-55. */
+AK_API int ak_row_sumsq(const void* x, int64_t rows, int64_t cols, int64_t ld, int dtype,
+                 float* ss_out, void* stream);
+AK_API int ak_linear_rms(const void* x, const void* w, void* C, const void* R, int64_t M,
+                  int64_t N, int64_t K, int64_t ldx, int64_t ldc, int64_t ldr,
+                  const float* rs_in, int rs_tiles, float eps, float* ss_out, int dtype,
+                  void* stream);
+AK_API int ak_mlp_gate_up_rms(const void* x, const void* w_gate, const void* w_up, void* hidden,
+                       int64_t M, int64_t D, int64_t H, const float* rs_in, int rs_tiles,
+                       float eps, int activation, int dtype, void* stream);
+
 /* out[M, D] = (act(x @ w_gate^T) * (x @ w_up^T)) @ w_down^T with w_down
  * [D, H]; `hidden` is caller workspace of M*H elements of dtype.
  * Replaces kernels/fused_mlp.py:102 kernel_fn(x, w_gate, w_up, w_down,

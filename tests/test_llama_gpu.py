@@ -34,17 +34,25 @@ def test_reference_weights_tiny(dtype):
     check(logits, _oracle_logits(m, g["cfg"], g["tokens"]), "matmul", "llama tiny", scale_tol=2.0)
 
 
+@pytest.mark.parametrize("fuse_norms", [True, False])
 @pytest.mark.parametrize("dtype,scale_tol", [(torch.float16, 2.0), (torch.bfloat16, 10.0)])
 @pytest.mark.parametrize("n_kv", [4, 1])
-def test_tensor_core_attention_config(n_kv, dtype, scale_tol):
-    """head_dim 128: projections, RoPE and attention all take the tensor-core paths.  The
-    residual stream is stored in the model dtype between layers, so bf16 (7 mantissa bits)
-    accumulates about 8x the error of fp16 (10 bits) over the two layers: measured max logit
-    error 0.010 (fp16) and 0.09 (bf16) on logits of standard deviation 1.1."""
+def test_tensor_core_attention_config(n_kv, dtype, scale_tol, fuse_norms):
+    """head_dim 128: projections, RoPE and attention all take the tensor-core paths, with the
+    RMSNorms folded into the projections (fuse_norms) or run as their own kernel; the norm
+    weights are 1 + 0.1 N(0,1), so the folding is exercised.  The residual stream is stored in
+    the model dtype between layers, so bf16 (7 mantissa bits) accumulates about 8x the error of
+    fp16 (10 bits) over the two layers: measured max logit error 0.010 (fp16) and 0.09 (bf16)
+    on logits of standard deviation 1.1."""
     from autokernel_b200.llama import LlamaB200, LlamaConfig
     cfg = dict(vocab_size=512, dim=512, n_layers=2, n_heads=4, n_kv_heads=n_kv, hidden_dim=1024)
     c = LlamaConfig(**cfg)
-    m = LlamaB200(c, LlamaB200.random_weights(c, "cuda", dtype=dtype, seed=3, std=0.05))
+    w = LlamaB200.random_weights(c, "cuda", dtype=dtype, seed=3, std=0.05)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    for k in w:
+        if k.endswith("norm.weight"):
+            w[k] = (1 + 0.1 * torch.randn(w[k].shape, device="cuda", generator=g)).to(dtype)
+    m = LlamaB200(c, w, fuse_norms=fuse_norms)
     tokens = torch.randint(0, 512, (2, 320), generator=torch.Generator().manual_seed(4))
     logits = m(tokens.cuda())
     ref = _oracle_logits(m, cfg, tokens)
