@@ -28,7 +28,6 @@ SIGNATURES = {
     "ak_device_status": (_i32, [_i32]),
     "ak_sm_count": (_i32, []),
     "ak_set_force_simt": (None, [_i32]),
-    "ak_set_gemm_pair": (None, [_i32]),
     "ak_rmsnorm": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
     "ak_rmsnorm_fp32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
     "ak_layernorm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),

@@ -73,11 +73,6 @@ bool make_tmap(CUtensorMap* map, int dtype, int rank, const void* base, const ui
   return true;
 }
 
-int g_gemm_pair = [] {
-  const char* e = getenv("AK_GEMM_PAIR");
-  return (e && e[0] == '1') ? 1 : 0;
-}();
-
 namespace gemm {
 
 using namespace sm100;
@@ -439,208 +434,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-// ------------------------------------------------------------------ 2-SM variant
-// A cluster of two CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2
-// (M = 256 split 128 / 128 over the pair, N = 256 split 128 / 128 over the pair's
-// shared-memory B halves).  Per CTA and stage: A 128 x 64 + B 128 x 64 (32 KiB), so
-// six stages fit and each SM streams a third less operand data per FLOP than the
-// 1-SM kernel.  CTA 0 of the pair issues the MMAs; both CTAs' producers load their
-// halves with completion counted on CTA 0's stage barrier; CTA 0 commits to both
-// CTAs' stage-free and accumulator-ready barriers; both epilogues drain their own
-// TMEM rows and report to CTA 0.
-constexpr int P_STAGES = 6;
-constexpr int P_A_BYTES = 128 * BK * 2;  // 16 KB
-constexpr int P_B_BYTES = 128 * BK * 2;  // 16 KB: this CTA's half of the N = 256 columns
-constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024;
-
-AK_D void pair_tile_coords(int t, const Params& p, int& tm, int& tn) {
-  // p.tiles_m counts 256-row pair tiles here
-  tile_coords(t, p, tm, tn);
-}
-
-template <int DT, int MODE>
-__global__ void __launch_bounds__(THREADS, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                     const __grid_constant__ CUtensorMap tb2, Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~(uintptr_t)1023);
-  __shared__ uint64_t full[P_STAGES], empty[P_STAGES], acc_full[2], acc_empty[2];
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
-  const bool leader = rank == 0;
-  const int pair = (int)cluster_id_x(), npairs = (int)n_clusters_x();
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < P_STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);  // 4 epilogue warps in each CTA of the pair
-    }
-    abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&ta);
-    tma_prefetch_desc(&tb);
-    if (MODE == MODE_DUAL) tma_prefetch_desc(&tb2);
-  }
-  if (warp == 1) {
-    tmem_alloc_pair(&tmem_slot, TMEM_COLS);
-    tmem_relinquish_pair();
-  }
-  tc_fence_before();
-  cluster_sync();  // both CTAs' barriers exist before anyone signals a peer
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  volatile int* abort_p = &abort_flag;
-  const int nk = (p.K + BK - 1) / BK;
-
-  if (warp == 0) {
-    if (lane == 0) {  // ---------------- TMA producer (both CTAs)
-      int s = 0;
-      uint32_t ph = 0;
-      bool ok = true;
-      for (int t = pair; ok && t < p.num_tiles; t += npairs) {
-        int tm, tn;
-        pair_tile_coords(t, p, tm, tn);
-        const int m0 = tm * 256 + (int)rank * 128;
-        for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&empty[s], ph ^ 1, abort_p)) {
-            ok = false;
-            break;
-          }
-          uint8_t* sa = smem + s * P_STAGE_BYTES;
-          uint8_t* sb = sa + P_A_BYTES;
-          if (leader) mbar_expect_tx(&full[s], 2 * P_STAGE_BYTES);
-          const int k0 = kb * BK;
-          tma_load_2d_pair(sa, &ta, &full[s], k0, m0);
-          if (MODE == MODE_K) {
-            tma_load_2d_pair(sb, &tb, &full[s], k0, tn * 256 + (int)rank * 128);
-          } else if (MODE == MODE_DUAL) {  // CTA 0: gate rows, CTA 1: up rows
-            tma_load_2d_pair(sb, rank == 0 ? &tb : &tb2, &full[s], k0, tn * 128);
-          } else {
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-              tma_load_2d_pair(sb + c * (64 * BK * 2), &tb, &full[s],
-                               tn * 256 + (int)rank * 128 + c * 64, k0);
-          }
-          if (++s == P_STAGES) {
-            s = 0;
-            ph ^= 1;
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && leader) {  // ---------------- MMA issuer (CTA 0 only)
-      uint32_t empty_peer[P_STAGES], accf_peer[2];
-      for (int s = 0; s < P_STAGES; ++s) empty_peer[s] = map_to_rank(&empty[s], 1);
-      for (int b = 0; b < 2; ++b) accf_peer[b] = map_to_rank(&acc_full[b], 1);
-      int s = 0;
-      uint32_t ph = 0;
-      bool ok = true;
-      int it = 0;
-      for (int t = pair; ok && t < p.num_tiles; t += npairs, ++it) {
-        const int b = it & 1;
-        const uint32_t aph = (it >> 1) & 1;
-        if (!mbar_wait(&acc_empty[b], aph ^ 1, abort_p)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + b * BN;
-        for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_p)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * P_STAGE_BYTES);
-          const uint32_t sb = sa + P_A_BYTES;
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = desc_kmajor(sa + k * 32);
-            const uint64_t bd = (MODE == MODE_MN) ? desc_mnmajor(sb + k * 16 * 128, 64 * BK * 2)
-                                                  : desc_kmajor(sb + k * 32);
-            umma_ss_pair(d, ad, bd, p.idesc, (kb | k) != 0);
-          }
-          umma_commit_pair(smem_u32(&empty[s]));
-          umma_commit_pair(empty_peer[s]);
-          if (++s == P_STAGES) {
-            s = 0;
-            ph ^= 1;
-          }
-        }
-        if (ok) {
-          umma_commit_pair(smem_u32(&acc_full[b]));
-          umma_commit_pair(accf_peer[b]);
-        }
-      }
-    }
-  } else {  // ---------------- epilogue warps 2..5 (both CTAs, own TMEM rows)
-    const int q = warp & 3;
-    const uint32_t acce_leader0 = map_to_rank(&acc_empty[0], 0);
-    const uint32_t acce_leader1 = map_to_rank(&acc_empty[1], 0);
-    int it = 0;
-    for (int t = pair; t < p.num_tiles; t += npairs, ++it) {
-      const int b = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
-      int ok = 0;
-      if (lane == 0) ok = mbar_wait(&acc_full[b], aph, abort_p) ? 1 : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      tc_fence_after();
-      int tm, tn;
-      pair_tile_coords(t, p, tm, tn);
-      const int row = tm * 256 + (int)rank * 128 + q * 32 + lane;
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * BN;
-      if (MODE != MODE_DUAL) {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c, r);
-          tmem_wait_ld();
-          tmem_regs_ready(r);
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          rope_row32(p, row, tn * BN + c, v);
-          store_row32<DT>(p, row, tn * BN + c, v);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(tbase + c, g);
-          tmem_ld32(tbase + BN / 2 + c, u);
-          tmem_wait_ld();
-          tmem_regs_ready(g);
-          tmem_regs_ready(u);
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = swiglu_ref<DT>(p.act, __uint_as_float(g[j]), __uint_as_float(u[j]));
-          store_row32<DT>(p, row, tn * (BN / 2) + c, v);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(b ? acce_leader1 : acce_leader0);
-    }
-  }
-  tc_fence_before();
-  cluster_sync();  // neither CTA leaves (or frees TMEM) while its peer may still signal it
-  if (warp == 1) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, TMEM_COLS);
-  }
-}
-
 template <int DT, int MODE>
 static int launch(const void* A, const void* B, const void* B2, void* C, int M, int N, int K,
                   int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R, int64_t ldr,
@@ -706,82 +499,6 @@ static int launch(const void* A, const void* B, const void* B2, void* C, int M, 
   return launch_status("tc_gemm");
 }
 
-template <int DT, int MODE>
-static int launch_pair(const void* A, const void* B, const void* B2, void* C, int M, int N,
-                       int K, int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R,
-                       int64_t ldr, const RopeEpilogue& rope, cudaStream_t st) {
-  CUtensorMap ta, tb, tb2;
-  {
-    uint64_t dims[2] = {(uint64_t)K, (uint64_t)M}, str[1] = {(uint64_t)lda * 2};
-    uint32_t box[2] = {BK, 128};
-    if (!make_tmap(&ta, DT, 2, A, dims, str, box)) return AK_ERR_LAUNCH;
-  }
-  if (MODE == MODE_MN) {
-    uint64_t dims[2] = {(uint64_t)N, (uint64_t)K}, str[1] = {(uint64_t)ldb * 2};
-    uint32_t box[2] = {64, BK};
-    if (!make_tmap(&tb, DT, 2, B, dims, str, box)) return AK_ERR_LAUNCH;
-    tb2 = tb;
-  } else {
-    uint64_t dims[2] = {(uint64_t)K, (uint64_t)N}, str[1] = {(uint64_t)ldb * 2};
-    uint32_t box[2] = {BK, 128};
-    if (!make_tmap(&tb, DT, 2, B, dims, str, box)) return AK_ERR_LAUNCH;
-    if (MODE == MODE_DUAL) {
-      if (!make_tmap(&tb2, DT, 2, B2, dims, str, box)) return AK_ERR_LAUNCH;
-    } else {
-      tb2 = tb;
-    }
-  }
-  Params p;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.C = C;
-  p.ldc = ldc;
-  p.tiles_m = (M + 255) / 256;
-  const int bn_out = MODE == MODE_DUAL ? BN / 2 : BN;
-  p.tiles_n = (N + bn_out - 1) / bn_out;
-  p.num_tiles = p.tiles_m * p.tiles_n;
-  p.act = act;
-  p.vec_store = (ldc % 8 == 0) && aligned16(C) && (!R || ((ldr % 8 == 0) && aligned16(R)));
-  p.R = R;
-  p.ldr = ldr;
-  p.rope_cos = rope.cos;
-  p.rope_sin = rope.sin;
-  p.rope_T = rope.T;
-  p.rope_hd = rope.head_dim;
-  p.rope_cols = rope.cols;
-  p.xt_targets = nullptr;
-  p.xt_part = nullptr;
-  p.xt_tgt = nullptr;
-  p.rs_in = nullptr;
-  p.rs_tiles = 0;
-  p.rs_inv_k = 1.f;
-  p.rs_eps = 0.f;
-  p.ss_out = nullptr;
-  p.idesc = sm100::idesc_f16(DT == AK_BF16 ? 1 : 0, 256, BN, false, MODE == MODE_MN);
-
-  const cudaError_t attr_err = smem_optin<gemm_pair_kernel<DT, MODE>>(P_SMEM_BYTES);
-  AK_REQUIRE(attr_err == cudaSuccess, AK_ERR_LAUNCH, "gemm pair: smem attribute: %s",
-             cudaGetErrorString(attr_err));
-  int pairs = device_info().sm_count / 2;
-  if (pairs > p.num_tiles) pairs = p.num_tiles;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = P_SMEM_BYTES;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<DT, MODE>, ta, tb, tb2, p);
-  AK_REQUIRE(e == cudaSuccess, AK_ERR_LAUNCH, "gemm pair launch: %s", cudaGetErrorString(e));
-  return launch_status("tc_gemm_pair");
-}
-
 }  // namespace gemm
 
 // Tensor-core eligibility: 16-bit types, TMA-describable operands (16-byte
@@ -799,16 +516,7 @@ int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, v
             int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act, const void* R,
             int64_t ldr, const RopeEpilogue& rope, cudaStream_t st) {
   using namespace gemm;
-  // The CTA-pair kernel is opt-in (ak_set_gemm_pair / AK_GEMM_PAIR=1): measured at the
-  // same throughput as the single-CTA kernel on the BASELINE shapes (both run at the
-  // power cap), so the simpler kernel stays the default.
-  const bool pair = M > 128 && g_gemm_pair;
 #define AK_TCG(D)                                                                               \
-  if (pair) {                                                                                   \
-    if (mode == MODE_K) return launch_pair<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st); \
-    if (mode == MODE_MN) return launch_pair<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st); \
-    return launch_pair<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st);             \
-  }                                                                                             \
   if (mode == MODE_K) return launch<D, MODE_K>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st);   \
   if (mode == MODE_MN) return launch<D, MODE_MN>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st); \
   return launch<D, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, rope, st);
@@ -848,4 +556,3 @@ int tc_gemm_xent(int dtype, const void* x, const void* w, int M, int N, int K, i
 
 }  // namespace ak
 
-extern "C" void ak_set_gemm_pair(int on) { ak::g_gemm_pair = on ? 1 : 0; }

@@ -231,143 +231,6 @@ AK_D void tmem_regs_ready(uint32_t* r) {
 }
 AK_D void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// ------------------------------------------------------------------ 2-SM (CTA pair) forms
-// A cluster of two CTAs shares one tcgen05.mma (cta_group::2): each CTA holds half of
-// the M rows of A and half of the N columns of B in its own shared memory at the same
-// offsets, and its half of the accumulator rows in its own TMEM.  None of these loads
-// use cluster multicast.
-AK_D uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-AK_D uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-AK_D uint32_t n_clusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-AK_D void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-// shared::cluster address of the same variable in CTA `rank` of the cluster
-AK_D uint32_t map_to_rank(const void* p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
-}
-// Arrive on a barrier of this CTA or its peer.  Default (CTA-scope release) semantics: a
-// cluster-scope release would put a full memory barrier in the arriving warp.  Callers
-// that publish TMEM contents order them with tcgen05.wait + tcgen05.fence first.
-AK_D void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-// TMA tile load into this CTA's shared memory whose completion is counted on the
-// barrier of CTA 0 of the pair (the peer bit of the barrier address cleared).
-AK_D void tma_load_2d_pair(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar) & 0xFEFFFFFFu), "r"(c0), "r"(c1)
-      : "memory");
-}
-AK_D void tma_load_4d_pair(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2,
-                           int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar) & 0xFEFFFFFFu), "r"(c0), "r"(c1),
-      "r"(c2), "r"(c3)
-      : "memory");
-}
-// Bounded wait whose acquire covers arrivals made by the peer CTA (release.cluster).
-AK_D bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-AK_D bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  while (true) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
-      *abort_flag = 1;
-      report_status(AK_STATUS_TIMEOUT);
-      return false;
-    }
-  }
-}
-AK_D void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                   smem_u32(slot)),
-               "r"(ncols)
-               : "memory");
-}
-AK_D void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-AK_D void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-AK_D void umma_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                       uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
-      : "memory");
-}
-// Arrive on the barrier at the same shared-memory offset in both CTAs of the pair when
-// the pair's previously issued MMAs complete (one commit per CTA).
-AK_D void umma_commit_pair_both(const void* bar) {
-  uint32_t peer;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, 1;" : "=r"(peer) : "r"(smem_u32(bar)));
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer)
-      : "memory");
-}
-// Named barrier over `threads` threads (a multiple of 32) of this CTA.
-AK_D void named_bar_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-// D[tmem] (+)= A[tmem] * B[smem] over the pair: each CTA supplies its half of the A rows
-// from its own TMEM and its half of the B columns from its own shared memory.
-AK_D void umma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                       uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc)
-      : "memory");
-}
-// Arrive on the barrier at shared::cluster address `cluster_addr` (this CTA's or the
-// peer's, from map_to_rank) once the pair's previously issued MMAs complete.
-AK_D void umma_commit_pair(uint32_t cluster_addr) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          cluster_addr)
-      : "memory");
-}
-
 }  // namespace sm100
 
 // Host side: encode a 2-D (or 3-D) tiled TMA descriptor with 128-byte

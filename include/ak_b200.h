@@ -60,10 +60,6 @@ AK_API int ak_device_status(int clear);
 AK_API int ak_sm_count(void);
 /* Test hook: 1 routes matmul/MLP/attention through the SIMT kernels. */
 AK_API void ak_set_force_simt(int on);
-/* 1 runs 16-bit matmul / MLP GEMMs with M > 128 on the CTA-pair (cta_group::2) tcgen05
- * kernel instead of the single-CTA one (also AK_GEMM_PAIR=1 at load time).  Same results
- * within rounding order of the accumulator; no reference counterpart (a kernel choice). */
-AK_API void ak_set_gemm_pair(int on);
 
 /* ----------------------------------------------------------------- row ops */
 

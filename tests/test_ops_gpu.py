@@ -431,30 +431,6 @@ def test_attention_wide_scores(dt):
     check(y, ref_f64.attention(to_np(q), to_np(k), to_np(v), False), "flash_attention", "wide")
 
 
-@pytest.mark.parametrize("dt", ["bf16", "f16"])
-@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (300, 520, 136), (1000, 768, 512)])
-def test_gemm_cta_pair_kernel(dt, M, N, K):
-    """The CTA-pair (cta_group::2) GEMM in its three modes matches the oracle."""
-    from autokernel_b200 import _lib
-    r = _gen(M * 3 + N)
-    A = r(M, K, scale=1 / math.sqrt(K)).to(DTS[dt])
-    B = r(K, N).to(DTS[dt])
-    W = r(N, K, scale=0.05).to(DTS[dt])
-    wg, wu, wd = (r(N, K, scale=0.05).to(DTS[dt]), r(N, K, scale=0.05).to(DTS[dt]),
-                  r(K, N, scale=0.05).to(DTS[dt]))
-    _lib.load().ak_set_gemm_pair(1)
-    try:
-        y1 = ops().matmul(A.to(DEV), B.to(DEV))
-        y2 = ops().matmul(A.to(DEV), W.to(DEV).t())
-        y3 = ops().fused_mlp(A.to(DEV), wg.to(DEV), wu.to(DEV), wd.to(DEV))
-        torch.cuda.synchronize()
-    finally:
-        _lib.load().ak_set_gemm_pair(0)
-    check(y1, ref_f64.matmul(to_np(A), to_np(B)), "matmul", "pair MN")
-    check(y2, ref_f64.matmul(to_np(A), to_np(W).T), "matmul", "pair K")
-    check(y3, ref_f64.fused_mlp(to_np(A), to_np(wg), to_np(wu), to_np(wd)), "fused_mlp", "pair dual")
-
-
 @pytest.mark.parametrize("rows,cols", [(64, 4096), (300, 1024), (8, 32768), (8000, 4096)])
 def test_layernorm_large_offset(rows, cols):
     """Mean far from zero (1000 + N(0,1)): the merged per-thread variance stays accurate."""
