@@ -307,11 +307,16 @@ def time_compute_ops(device, world, reps: int) -> dict:
     # 33.5 MB of input would sit in the 126 MB L2 between calls: rotate over 4 copies
     xs = [x] + [x.clone() for _ in range(3)]
     cyc = iter(range(1 << 30))
-    t, ck = timeit(lambda: ops.rmsnorm(xs[next(cyc) % 4], w, 1e-6), n=max(reps, 48))
-    del xs
+    # configs[0] states y = x * rsqrt(mean(x^2) + eps) * weight with fp32 accumulation: the
+    # one-rounding kernel; reference.py's per-operator rounding (kernel_fn) is timed beside it
     by = 2 * x.numel() * 2 + w.numel() * 2
-    res["rmsnorm_fp16_4096x4096"] = {"clocks": ck, "GB/s": by / t / 1e9, "frac_hbm": by / t / 1e9 / pk["hbm_gbs"], "us": t * 1e6,
-                                     "timing": "CUDA graph of 48 calls, inputs rotated over 4 buffers (134 MB > L2)"}
+    for name, fn in (("rmsnorm_fp16_4096x4096", ops.rmsnorm_fp32),
+                     ("rmsnorm_reference_rounding_fp16_4096x4096", ops.rmsnorm)):
+        t, ck = timeit(lambda: fn(xs[next(cyc) % 4], w, 1e-6), n=max(reps, 48))
+        res[name] = {"clocks": ck, "GB/s": by / t / 1e9, "frac_hbm": by / t / 1e9 / pk["hbm_gbs"],
+                     "us": t * 1e6,
+                     "timing": "CUDA graph of 48 calls, inputs rotated over 4 buffers (134 MB > L2)"}
+    del xs
     del x, w
     # cross entropy: LM-head shard at 8 GPUs, fp16 logits
     lg = torch.randn(W.XENT["rows"], W.XENT["vocab"], device=device, generator=g).half()
