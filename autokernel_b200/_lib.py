@@ -49,7 +49,7 @@ SIGNATURES = {
     "ak_linear_rope": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "ak_row_sumsq": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _vp]),
     "ak_linear_rms": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i32, _f32,
-                             _vp, _i32, _vp]),
+                             _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "ak_mlp_gate_up_rms": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _i32, _f32, _i32, _i32,
                                   _vp]),
     "ak_mlp_gate_up": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),

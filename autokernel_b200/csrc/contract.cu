@@ -239,7 +239,8 @@ static int rms_common_checks(const void* x, const void* w, int64_t M, int64_t N,
 extern "C" int ak_linear_rms(const void* x, const void* w, void* C, const void* R, int64_t M,
                              int64_t N, int64_t K, int64_t ldx, int64_t ldc, int64_t ldr,
                              const float* rs_in, int rs_tiles, float eps, float* ss_out,
-                             int dtype, void* stream) {
+                             const float* cos, const float* sin, int64_t T, int64_t head_dim,
+                             int64_t rope_cols, int dtype, void* stream) {
   int rc = rms_common_checks(x, w, M, N, K, ldx, dtype, rs_in, rs_tiles);
   if (rc) return rc;
   AK_REQUIRE(ldc >= N && (!R || ldr >= N), AK_ERR_SHAPE, "leading dimension too small");
@@ -250,8 +251,19 @@ extern "C" int ak_linear_rms(const void* x, const void* w, void* C, const void* 
   rms.rs_tiles = rs_tiles;
   rms.eps = eps;
   rms.ss_out = ss_out;
+  RopeEpilogue rope;
+  if (cos) {
+    AK_REQUIRE(sin && T > 0 && head_dim > 0 && head_dim % 2 == 0 && rope_cols >= 0 &&
+                   rope_cols <= N && rope_cols % head_dim == 0 && T < (1LL << 31),
+               AK_ERR_ARG, "bad RoPE epilogue arguments");
+    rope.cos = cos;
+    rope.sin = sin;
+    rope.T = (int)T;
+    rope.head_dim = (int)head_dim;
+    rope.cols = (int)rope_cols;
+  }
   return tc_gemm_rms(dtype, false, x, w, nullptr, C, (int)M, (int)N, (int)K, ldx, K, ldc, 0, R,
-                     ldr, rms, (cudaStream_t)stream);
+                     ldr, rms, rope, (cudaStream_t)stream);
 }
 
 extern "C" int ak_mlp_gate_up_rms(const void* x, const void* w_gate, const void* w_up,
@@ -270,5 +282,5 @@ extern "C" int ak_mlp_gate_up_rms(const void* x, const void* w_gate, const void*
   rms.rs_tiles = rs_tiles;
   rms.eps = eps;
   return tc_gemm_rms(dtype, true, x, w_gate, w_up, hidden, (int)M, (int)H, (int)D, D, D, H,
-                     activation, nullptr, 0, rms, (cudaStream_t)stream);
+                     activation, nullptr, 0, rms, RopeEpilogue(), (cudaStream_t)stream);
 }

@@ -34,7 +34,8 @@ constexpr int kRmsTileN = 256;
 
 int tc_gemm_rms(int dtype, bool dual, const void* A, const void* B, const void* B2, void* C,
                 int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act,
-                const void* R, int64_t ldr, const RmsEpilogue& rms, cudaStream_t st);
+                const void* R, int64_t ldr, const RmsEpilogue& rms, const RopeEpilogue& rope,
+                cudaStream_t st);
 
 int tc_gemm_xent(int dtype, const void* x, const void* w, int M, int N, int K, int64_t ldx,
                  int64_t ldw, const XentEpilogue& xe, cudaStream_t st);

@@ -207,6 +207,27 @@ AK_D void rope_row32(const Params& p, int row, int col, float* v) {
   if (!p.rope_cos || col >= p.rope_cols || row >= p.M) return;
   const int t = row % p.rope_T;
   const int half = p.rope_hd >> 1;
+  if ((p.rope_hd & 31) == 0 && col + 32 <= p.rope_cols && (half & 3) == 0 &&
+      ((reinterpret_cast<uintptr_t>(p.rope_cos) | reinterpret_cast<uintptr_t>(p.rope_sin)) & 15) == 0) {
+    // a 32-column chunk lies inside one head: its 16 pairs use 16 consecutive table entries,
+    // read as float4s (the table rows are 16-byte aligned when head_dim / 2 is a multiple of 4)
+    const int i0 = (col % p.rope_hd) >> 1;
+    const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + (int64_t)t * half + i0);
+    const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + (int64_t)t * half + i0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 c4 = __ldg(cs + q), s4 = __ldg(sn + q);
+      const float co[4] = {c4.x, c4.y, c4.z, c4.w}, si[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int jj = q * 4 + e;
+        const float x1 = v[2 * jj], x2 = v[2 * jj + 1];
+        v[2 * jj] = fmaf(x1, co[e], -x2 * si[e]);
+        v[2 * jj + 1] = fmaf(x1, si[e], x2 * co[e]);
+      }
+    }
+    return;
+  }
   const float* cs = p.rope_cos + (int64_t)t * half;
   const float* sn = p.rope_sin + (int64_t)t * half;
 #pragma unroll
@@ -527,9 +548,9 @@ int tc_gemm(int dtype, int mode, const void* A, const void* B, const void* B2, v
 
 int tc_gemm_rms(int dtype, bool dual, const void* A, const void* B, const void* B2, void* C,
                 int M, int N, int K, int64_t lda, int64_t ldb, int64_t ldc, int act,
-                const void* R, int64_t ldr, const RmsEpilogue& rms, cudaStream_t st) {
+                const void* R, int64_t ldr, const RmsEpilogue& rms, const RopeEpilogue& none,
+                cudaStream_t st) {
   using namespace gemm;
-  const RopeEpilogue none;
   if (dtype == AK_BF16) {
     if (dual)
       return launch<AK_BF16, MODE_DUAL>(A, B, B2, C, M, N, K, lda, ldb, ldc, act, R, ldr, none,

@@ -86,6 +86,8 @@ class LlamaB200:
         dt = weights["tok_embeddings.weight"].dtype
         # RMSNorm folded into the projections after it (16-bit weights: tensor-core GEMMs)
         self.fuse_norms = dt in (torch.float16, torch.bfloat16) if fuse_norms is None else fuse_norms
+        # with folded norms, RoPE of q and k runs in their projection GEMMs' epilogue
+        self.fuse_rope = self.fuse_norms
         self._folded: dict[int, tuple] = {}
 
     @staticmethod
@@ -183,11 +185,13 @@ class LlamaB200:
         B, T, _ = h.shape
         hd, eps = c.head_dim, c.norm_eps
         wq, wk, wv, w1, w3 = self._fold(i)
-        q = ops.linear_rms(h, wq, ss, eps).view(B, T, c.n_heads, hd)
-        k = ops.linear_rms(h, wk, ss, eps).view(B, T, c.n_kv_heads, hd)
+        rope = (cos, sin, T, hd) if self.fuse_rope else None
+        q = ops.linear_rms(h, wq, ss, eps, rope=rope).view(B, T, c.n_heads, hd)
+        k = ops.linear_rms(h, wk, ss, eps, rope=rope).view(B, T, c.n_kv_heads, hd)
         v = ops.linear_rms(h, wv, ss, eps).view(B, T, c.n_kv_heads, hd)
-        q = ops.rope_apply(q, cos, sin)
-        k = ops.rope_apply(k, cos, sin)
+        if not self.fuse_rope:
+            q = ops.rope_apply(q, cos, sin)
+            k = ops.rope_apply(k, cos, sin)
         o = self._attention(q, k, v, B, T)
         _, ss = ops.linear_rms(o.view(B, T, c.n_heads * hd), w[p + "attention.wo.weight"],
                                residual=h, out=h, want_ss=True)

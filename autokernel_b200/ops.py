@@ -415,11 +415,13 @@ def fold_norm_weight(weight: torch.Tensor, norm_weight: torch.Tensor) -> torch.T
 
 def linear_rms(x: torch.Tensor, weight: torch.Tensor, rs: torch.Tensor | None = None,
                eps: float = 1e-6, residual: torch.Tensor | None = None,
-               out: torch.Tensor | None = None, want_ss: bool = False):
+               out: torch.Tensor | None = None, want_ss: bool = False, rope: tuple | None = None):
     """x @ weight^T with the rows scaled by 1 / sqrt(mean(x^2) + eps) from rs (the
     row_sumsq partials of x) -- RMSNorm(x) @ w^T when weight = fold_norm_weight(w, norm
     weight) -- plus an optional residual added in the epilogue (out may alias it).  With
-    want_ss also returns the partial sums of squares of the result, for the next norm."""
+    want_ss also returns the partial sums of squares of the result, for the next norm.  With
+    rope = (cos, sin, T, head_dim) -- fp32 tables [T, head_dim / 2] -- interleaved RoPE is applied
+    to every output column before rounding, row r at position r % T."""
     require_cuda(x, weight)
     x2 = _rows_view(x)
     M, K = x2.shape
@@ -431,11 +433,18 @@ def linear_rms(x: torch.Tensor, weight: torch.Tensor, rs: torch.Tensor | None = 
     ss = (torch.empty((N + RMS_TILE - 1) // RMS_TILE, M, dtype=torch.float32, device=x.device)
           if want_ss else None)
     r = residual
+    c = s_ = None
+    T = hd = 0
+    if rope is not None:
+        c, s_, T, hd = rope
+        c = c.reshape(T, hd // 2).float().contiguous()
+        s_ = s_.reshape(T, hd // 2).float().contiguous()
     call("ak_linear_rms", x2.data_ptr(), weight.data_ptr(), o.data_ptr(),
          r.data_ptr() if r is not None else None, M, N, K, x2.stride(0), N, N,
          rs.data_ptr() if rs is not None else None, rs.shape[0] if rs is not None else 0,
-         float(eps), ss.data_ptr() if ss is not None else None, dtype_code(x.dtype),
-         stream_ptr(x.device))
+         float(eps), ss.data_ptr() if ss is not None else None,
+         c.data_ptr() if c is not None else None, s_.data_ptr() if s_ is not None else None,
+         T, hd, N if rope is not None else 0, dtype_code(x.dtype), stream_ptr(x.device))
     return (o, ss) if want_ss else o
 
 

@@ -209,7 +209,10 @@ AK_API int ak_mlp_gate_up(const void* x, const void* w_gate, const void* w_up, v
  *   ak_linear_rms:       C = rowscale * (x @ w^T) [+ R] with x [M, K], w [N, K]; rs_in
  *                        (optional) the rs_tiles partials of x; ss_out (optional) receives
  *                        the partials [ceil(N / 256)][M] of the stored C (after + R), for the
- *                        next norm.  R may alias C (in-place residual update).
+ *                        next norm.  R may alias C (in-place residual update).  With cos
+ *                        (optional) interleaved RoPE is applied to output columns
+ *                        [0, rope_cols) before rounding, as in ak_linear_rope (position
+ *                        row % T, fp32 cos/sin [T, head_dim / 2]).
  *   ak_mlp_gate_up_rms:  hidden = act(g) * u with g, u the row-scaled x @ w_gate^T,
  *                        x @ w_up^T (reference.py:45-55 rounding of the hidden).
  * 16-bit operands on the tensor-core path only (AK_ERR_ARG otherwise).  Fused neighbours of
@@ -219,7 +222,8 @@ AK_API int ak_row_sumsq(const void* x, int64_t rows, int64_t cols, int64_t ld, i
                  float* ss_out, void* stream);
 AK_API int ak_linear_rms(const void* x, const void* w, void* C, const void* R, int64_t M,
                   int64_t N, int64_t K, int64_t ldx, int64_t ldc, int64_t ldr,
-                  const float* rs_in, int rs_tiles, float eps, float* ss_out, int dtype,
+                  const float* rs_in, int rs_tiles, float eps, float* ss_out, const float* cos,
+                  const float* sin, int64_t T, int64_t head_dim, int64_t rope_cols, int dtype,
                   void* stream);
 AK_API int ak_mlp_gate_up_rms(const void* x, const void* w_gate, const void* w_up, void* hidden,
                        int64_t M, int64_t D, int64_t H, const float* rs_in, int rs_tiles,

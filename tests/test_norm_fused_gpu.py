@@ -73,3 +73,20 @@ def test_mlp_hidden_rms(dt):
                                ops().row_sumsq(x), 1e-6)
     xn = ref_f64.rmsnorm(to_np(x), to_np(wn), 1e-6)
     check(hid, ref_f64.mlp_hidden(xn, to_np(wg), to_np(wu)), "fused_mlp", "mlp_hidden_rms")
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_linear_rms_with_rope_epilogue(dt):
+    """q = RoPE(RMSNorm(h) @ Wq^T) in one GEMM: against the f64 oracle of the norm, projection
+    and interleaved rotation (models/llama_7b.py:40-48), position = row % T."""
+    B, T, D, hd = 2, 256, 512, 128
+    h = _r((B, T, D), 11, 1.0, dt)
+    wn = (1 + 0.1 * _r((D,), 12, 1.0, "bf16").float()).to(DTS[dt])
+    Wq = _r((D, D), 13, 0.05, dt)
+    c, s = ref_f64.cos_sin_table(T, hd // 2)
+    ct, st = torch.tensor(c, dtype=torch.float32, device=DEV), torch.tensor(s, dtype=torch.float32, device=DEV)
+    Wf = ops().fold_norm_weight(Wq, wn)
+    q = ops().linear_rms(h, Wf, ops().row_sumsq(h), 1e-6, rope=(ct, st, T, hd))
+    proj = (ref_f64.rmsnorm(to_np(h), np.ones(D), 1e-6) @ to_np(Wf).T).reshape(B, T, D // hd, hd)
+    e = ref_f64.rotary_embedding(proj, c[:, None, :], s[:, None, :]).reshape(B, T, D)
+    check(q, e, "matmul", "linear_rms + rope")
