@@ -49,6 +49,21 @@ AK_D float div_rn(float a, float b, float inv) {
   return r == r ? fmaf(r, inv, q0) : q0;
 }
 
+// Packed pairs of a 16-bit dtype.  A product of two 16-bit values is exact in fp32, so the
+// packed multiply, which rounds once, gives exactly ATen's float(a) * float(b) rounded to the
+// dtype: reference.py's x ** 2 and (x / rms) * w without unpacking.
+template <int DT> struct Pair16;
+template <> struct Pair16<AK_F16> {
+  using T2 = __half2;
+  static AK_D T2 pack(float a, float b) { return __floats2half2_rn(a, b); }
+  static AK_D float2 unpack(T2 v) { return __half22float2(v); }
+};
+template <> struct Pair16<AK_BF16> {
+  using T2 = __nv_bfloat162;
+  static AK_D T2 pack(float a, float b) { return __floats2bfloat162_rn(a, b); }
+  static AK_D float2 unpack(T2 v) { return __bfloat1622float2(v); }
+};
+
 // rms of reference.py:26-29 from the fp32 sum of the rounded squares: mean = sum * (1 / n)
 // (ATen's mean multiplies by the fp32 reciprocal of the count), then + eps and sqrt, each
 // rounded to the dtype.
@@ -117,13 +132,19 @@ __global__ void __launch_bounds__(1024) row_reg_kernel(RowArgs a) {
     float acc = 0.f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-      float f[VEC];
-      elems(i, f);
+      if constexpr (DT == AK_F32) {
+        float f[VEC];
+        elems(i, f);
 #pragma unroll
-      for (int j = 0; j < VEC; j += 2) {
-        float p = f[j] * f[j], q = f[j + 1] * f[j + 1];
-        rnd2<DT>(p, q);
-        acc += p + q;
+        for (int j = 0; j < VEC; ++j) acc = fmaf(f[j], f[j], acc);
+      } else {
+        using P = Pair16<DT>;
+        const typename P::T2* x2 = reinterpret_cast<const typename P::T2*>(&raw[i]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 sq = P::unpack(__hmul2(x2[k], x2[k]));  // x*x rounded to the dtype
+          acc += sq.x + sq.y;
+        }
       }
     }
     acc = rsum(acc);
@@ -196,14 +217,23 @@ __global__ void __launch_bounds__(1024) row_reg_kernel(RowArgs a) {
 #pragma unroll
       for (int j = 0; j < VEC; ++j) o[j] = (f[j] * s0) * wf[j];
     } else if (OP == OP_RMS_REF) {
-      float wf[VEC];
-      load_vec<DT>(w + v * VEC, wf);
+      if constexpr (DT == AK_F32) {
+        float wf[VEC];
+        load_vec<DT>(w + v * VEC, wf);
 #pragma unroll
-      for (int j = 0; j < VEC; j += 2) {
-        float p = div_rn(f[j], s0, s1), q = div_rn(f[j + 1], s0, s1);
-        rnd2<DT>(p, q);
-        o[j] = p * wf[j];
-        o[j + 1] = q * wf[j + 1];
+        for (int j = 0; j < VEC; ++j) o[j] = div_rn(f[j], s0, s1) * wf[j];
+      } else {
+        // rounded x / rms times w, rounded: one packed multiply per pair, stored as is
+        using P = Pair16<DT>;
+        const uint4 wraw = __ldg(reinterpret_cast<const uint4*>(w + v * VEC));
+        const typename P::T2* w2 = reinterpret_cast<const typename P::T2*>(&wraw);
+        uint4 out;
+        typename P::T2* y2 = reinterpret_cast<typename P::T2*>(&out);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          y2[k] = __hmul2(P::pack(div_rn(f[2 * k], s0, s1), div_rn(f[2 * k + 1], s0, s1)), w2[k]);
+        *reinterpret_cast<uint4*>(yr + v * VEC) = out;
+        continue;
       }
     } else if (OP == OP_LN) {
       float wf[VEC], bf[VEC];
