@@ -88,9 +88,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int q0 = qblk * 2 * BQ;
   // key blocks this CTA needs: all of them, or up to the diagonal of its last row
   int n_kv = (p.Sk + BKV - 1) / BKV;
+  // tile 0 (the first 128 rows) may need fewer: under the causal mask the block holding the
+  // diagonal of tile 1 is entirely above tile 0's rows
+  int n_kv0 = n_kv;
   if (p.causal) {
     const int last_row = min(q0 + 2 * BQ, p.Sq) - 1;
     n_kv = min(n_kv, last_row / BKV + 1);
+    n_kv0 = min(n_kv, (min(q0 + BQ, p.Sq) - 1) / BKV + 1);
   }
 
   if (threadIdx.x == 0) {
@@ -173,17 +177,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       for (int j = 0; ok && j < n_kv; ++j) {
         const int st = j & 1;
+        bool v_ready = false, k_ready = false;  // waited for V_j / K_{j+1} in this block
         for (int x = 0; x < 2 && ok; ++x) {
+          const int nx = x == 0 ? n_kv0 : n_kv;  // key blocks of tile x
+          if (j >= nx) continue;
           if (!mbar_wait(&p_full[x], j & 1, abort_p)) { ok = false; break; }
-          if (x == 0 && !mbar_wait(&v_full[st], (j >> 1) & 1, abort_p)) { ok = false; break; }
+          if (!v_ready && !mbar_wait(&v_full[st], (j >> 1) & 1, abort_p)) { ok = false; break; }
+          v_ready = true;
           tc_fence_after();
           pv(x, st, j > 0);
-          if (x == 1) umma_commit(&kv_empty[st]);
-          if (j == n_kv - 1) {
+          if (x == 1) umma_commit(&kv_empty[st]);  // tile 1 takes every block
+          if (j == nx - 1) {
             umma_commit(&o_done[x]);
           } else {
             const int nst = (j + 1) & 1;
-            if (x == 0 && !mbar_wait(&k_full[nst], ((j + 1) >> 1) & 1, abort_p)) { ok = false; break; }
+            if (!k_ready && !mbar_wait(&k_full[nst], ((j + 1) >> 1) & 1, abort_p)) { ok = false; break; }
+            k_ready = true;
             tc_fence_after();
             qk(x, nst);
             umma_commit(&s_full[x]);
@@ -202,7 +211,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     float m_ref = -INFINITY, l = 0.f;
     float rmax_raw = -INFINITY;  // the row's largest visible raw score
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
+    const int nx = x == 0 ? n_kv0 : n_kv;  // key blocks of this tile
+    for (int j = 0; j < nx; ++j) {
       int w = 0;
       if (lane == 0) w = mbar_wait(&s_full[x], j & 1, abort_p) ? 1 : 0;
       if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
