@@ -5,9 +5,10 @@
 // Q/K/V/O may be strided views [batch, heads, seq, D] (e.g. the [B, T, H, D]
 // projection outputs of a transformer read in place); K/V may have fewer heads
 // (grouped-query attention: query head h reads key/value head h / (H / Hkv)).
-// One CTA owns two 128-row query tiles (A, B) of one (batch, head) and walks the
-// key/value sequence in 128-key blocks.  320 threads, warp-specialised:
-//   warp 0      TMA producer: Q tiles once, then a 2-stage ring of {K, V} blocks
+// Persistent: one CTA per SM walks a static list of work items.  An item is two 128-row
+// query tiles (A, B) of one (batch, head); the CTA walks that item's key/value sequence in
+// 128-key blocks.  320 threads, warp-specialised:
+//   warp 0      TMA producer: each item's Q tiles, then a 2-stage ring of {K, V} blocks
 //               (4-D tensor maps [B, H, S, D], so tails zero-fill inside a head)
 //   warp 1      TMEM allocator (512 columns) + single-thread MMA issuer
 //   warps 2..5  softmax / epilogue of tile A, one thread per query row
@@ -62,8 +63,49 @@ struct Params {
   float ovf;         // |raw score| at which reference.py's 16-bit scores overflow (inf: none)
   uint32_t idesc_qk, idesc_pv;
   int n_qblk;        // query blocks of 256 rows
+  int n_items;       // n_qblk * batch * heads
 };
 
+// One work item = two 128-row query tiles (one query block) of one (batch, head).
+struct Item {
+  int b, h, hk, q0, n_kv, n_kv0;  // n_kv0: key blocks of the first tile (causal: may be fewer)
+};
+
+AK_D Item item_of(const Params& p, int it) {
+  // head-major, heavy (late, causal) query blocks first within each head: consecutive items
+  // share a head's K/V blocks in L2
+  Item t;
+  const int bh = it / p.n_qblk;
+  t.b = bh / p.H;
+  t.h = bh % p.H;
+  t.hk = t.h / p.rep;
+  const int qblk = p.n_qblk - 1 - (it - bh * p.n_qblk);
+  t.q0 = qblk * 2 * BQ;
+  // key blocks the item needs: all of them, or up to the diagonal of its last row; the first
+  // tile stops one block earlier when the second tile's diagonal block lies above all its rows
+  t.n_kv = (p.Sk + BKV - 1) / BKV;
+  t.n_kv0 = t.n_kv;
+  if (p.causal) {
+    t.n_kv = min(t.n_kv, (min(t.q0 + 2 * BQ, p.Sq) - 1) / BKV + 1);
+    t.n_kv0 = min(t.n_kv, (min(t.q0 + BQ, p.Sq) - 1) / BKV + 1);
+  }
+  return t;
+}
+
+// Item of this CTA's k-th round, or -1: CTAs walk the item list in rounds of gridDim.x items,
+// forwards in even rounds and backwards in odd ones, which balances the causal work (heavy and
+// light query blocks alternate) to within ~1% without any global counter.
+AK_D int item_index(const Params& p, int k) {
+  const int G = (int)gridDim.x, c = (int)blockIdx.x;
+  const int it = k * G + ((k & 1) ? G - 1 - c : c);
+  return it < p.n_items ? it : -1;
+}
+
+// Persistent: one CTA per SM walks its items; TMEM, barriers and the K/V ring stay live across
+// items, and the phases of every barrier follow running counters (items, key blocks per tile,
+// ring slots).  The next item's Q is loaded as soon as the current item's last Q K^T is done
+// (q_empty), and an item's first P V waits until the previous item's epilogue has read O
+// (o_free), so one item's tail overlaps the next one's start.
 template <int DT, int D>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -74,31 +116,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
-  __shared__ uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], o_done[2];
+  __shared__ uint64_t q_full, q_empty, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2],
+      o_done[2], o_free[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Consecutive CTAs take the query blocks of one (batch, head), so the K/V blocks they
-  // all stream are shared in L2; heavy (late, causal) query blocks are dispatched first
-  // within each head.
-  const int bh = (int)blockIdx.y;
-  const int b = bh / p.H, h = bh % p.H, hk = h / p.rep;
-  const int qblk = p.n_qblk - 1 - (int)blockIdx.x;
-  const int q0 = qblk * 2 * BQ;
-  // key blocks this CTA needs: all of them, or up to the diagonal of its last row
-  int n_kv = (p.Sk + BKV - 1) / BKV;
-  // tile 0 (the first 128 rows) may need fewer: under the causal mask the block holding the
-  // diagonal of tile 1 is entirely above tile 0's rows
-  int n_kv0 = n_kv;
-  if (p.causal) {
-    const int last_row = min(q0 + 2 * BQ, p.Sq) - 1;
-    n_kv = min(n_kv, last_row / BKV + 1);
-    n_kv0 = min(n_kv, (min(q0 + BQ, p.Sq) - 1) / BKV + 1);
-  }
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
+    mbar_init(&q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
@@ -106,6 +133,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
+      mbar_init(&o_free[i], 4);
     }
     abort_flag = 0;
     fence_mbar_init();
@@ -127,22 +155,31 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // ------------------------------------------ TMA producer
-      mbar_expect_tx(&q_full, 2 * C::TILE_BYTES);
-      for (int x = 0; x < 2; ++x)
-        for (int c = 0; c < C::NC; ++c)
-          tma_load_4d(smem + C::Q_OFF + x * C::TILE_BYTES + c * CHUNK_BYTES, &tq, &q_full, c * 64,
-                      q0 + x * BQ, h, b);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, abort_p)) break;
-        mbar_expect_tx(&k_full[st], C::TILE_BYTES);
-        for (int c = 0; c < C::NC; ++c)
-          tma_load_4d(smem + C::K_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tk, &k_full[st],
-                      c * 64, j * BKV, hk, b);
-        mbar_expect_tx(&v_full[st], C::TILE_BYTES);
-        for (int c = 0; c < C::NC; ++c)
-          tma_load_4d(smem + C::V_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tv, &v_full[st],
-                      c * 64, j * BKV, hk, b);
+      bool ok = true;
+      int g = 0;  // K/V ring slots used so far
+      for (int k = 0; ok; ++k) {
+        const int it = item_index(p, k);
+        if (it < 0) break;
+        const Item t = item_of(p, it);
+        // Q of this item once the previous item's last Q K^T has read the old one
+        if (k > 0 && !mbar_wait(&q_empty, (k - 1) & 1, abort_p)) break;
+        mbar_expect_tx(&q_full, 2 * C::TILE_BYTES);
+        for (int x = 0; x < 2; ++x)
+          for (int c = 0; c < C::NC; ++c)
+            tma_load_4d(smem + C::Q_OFF + x * C::TILE_BYTES + c * CHUNK_BYTES, &tq, &q_full,
+                        c * 64, t.q0 + x * BQ, t.h, t.b);
+        for (int j = 0; j < t.n_kv; ++j, ++g) {
+          const int st = g & 1;
+          if (!mbar_wait(&kv_empty[st], ((g >> 1) & 1) ^ 1, abort_p)) { ok = false; break; }
+          mbar_expect_tx(&k_full[st], C::TILE_BYTES);
+          for (int c = 0; c < C::NC; ++c)
+            tma_load_4d(smem + C::K_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tk, &k_full[st],
+                        c * 64, j * BKV, t.hk, t.b);
+          mbar_expect_tx(&v_full[st], C::TILE_BYTES);
+          for (int c = 0; c < C::NC; ++c)
+            tma_load_4d(smem + C::V_OFF + st * C::TILE_BYTES + c * CHUNK_BYTES, &tv, &v_full[st],
+                        c * 64, j * BKV, t.hk, t.b);
+        }
       }
     }
   } else if (warp == 1) {
@@ -167,35 +204,47 @@ __global__ void __launch_bounds__(THREADS, 1)
           umma_ts(d, a + kk * 8, desc_mnmajor(sv + st * C::TILE_BYTES + kk * 16 * 128, CHUNK_BYTES),
                   p.idesc_pv, (acc || kk > 0) ? 1 : 0);
       };
-      bool ok = mbar_wait(&q_full, 0, abort_p) && mbar_wait(&k_full[0], 0, abort_p);
-      if (ok) {
+      bool ok = true;
+      int g = 0;               // K/V ring slots consumed so far
+      int cnt[2] = {0, 0};     // key blocks processed so far by each tile (S / P phases)
+      for (int k = 0; ok; ++k) {
+        const int it = item_index(p, k);
+        if (it < 0) break;
+        const Item t = item_of(p, it);
+        if (!mbar_wait(&q_full, k & 1, abort_p) || !mbar_wait(&k_full[g & 1], (g >> 1) & 1, abort_p)) break;
         tc_fence_after();
-        qk(0, 0);
+        // S of both tiles for block 0 (the previous item's P V, issued earlier, has read S)
+        qk(0, g & 1);
         umma_commit(&s_full[0]);
-        qk(1, 0);
+        qk(1, g & 1);
         umma_commit(&s_full[1]);
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j & 1;
-        bool v_ready = false, k_ready = false;  // waited for V_j / K_{j+1} in this block
-        for (int x = 0; x < 2 && ok; ++x) {
-          const int nx = x == 0 ? n_kv0 : n_kv;  // key blocks of tile x
-          if (j >= nx) continue;
-          if (!mbar_wait(&p_full[x], j & 1, abort_p)) { ok = false; break; }
-          if (!v_ready && !mbar_wait(&v_full[st], (j >> 1) & 1, abort_p)) { ok = false; break; }
-          v_ready = true;
-          tc_fence_after();
-          pv(x, st, j > 0);
-          if (x == 1) umma_commit(&kv_empty[st]);  // tile 1 takes every block
-          if (j == nx - 1) {
-            umma_commit(&o_done[x]);
-          } else {
-            const int nst = (j + 1) & 1;
-            if (!k_ready && !mbar_wait(&k_full[nst], ((j + 1) >> 1) & 1, abort_p)) { ok = false; break; }
-            k_ready = true;
+        if (t.n_kv == 1) umma_commit(&q_empty);  // that was the item's last read of Q
+        for (int j = 0; ok && j < t.n_kv; ++j, ++g) {
+          const int st = g & 1;
+          bool v_ready = false, k_ready = false;  // waited for V_j / K_{j+1} in this block
+          for (int x = 0; x < 2 && ok; ++x) {
+            const int nx = x == 0 ? t.n_kv0 : t.n_kv;  // key blocks of tile x
+            if (j >= nx) continue;
+            if (!mbar_wait(&p_full[x], cnt[x] & 1, abort_p)) { ok = false; break; }
+            // the item's first P V overwrites O: the previous item's epilogue must have read it
+            if (j == 0 && k > 0 && !mbar_wait(&o_free[x], (k - 1) & 1, abort_p)) { ok = false; break; }
+            if (!v_ready && !mbar_wait(&v_full[st], (g >> 1) & 1, abort_p)) { ok = false; break; }
+            v_ready = true;
             tc_fence_after();
-            qk(x, nst);
-            umma_commit(&s_full[x]);
+            pv(x, st, j > 0);
+            ++cnt[x];
+            if (x == 1) umma_commit(&kv_empty[st]);  // tile 1 takes every block
+            if (j == nx - 1) {
+              umma_commit(&o_done[x]);
+            } else {
+              const int ng = g + 1;
+              if (!k_ready && !mbar_wait(&k_full[ng & 1], (ng >> 1) & 1, abort_p)) { ok = false; break; }
+              k_ready = true;
+              tc_fence_after();
+              qk(x, ng & 1);
+              umma_commit(&s_full[x]);
+              if (x == 1 && j + 1 == t.n_kv - 1) umma_commit(&q_empty);  // last read of Q
+            }
           }
         }
       }
@@ -204,110 +253,128 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int x = (warp - 2) >> 2;       // query tile 0 (warps 2..5) or 1 (warps 6..9)
     const int quarter = warp & 3;        // TMEM lanes this warp may access
     const int row_in_tile = quarter * 32 + lane;
-    const int qrow = q0 + x * BQ + row_in_tile;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t t_s = tmem + x * C::TMEM_TILE + lane_base;
     const uint32_t t_o = t_s + 128;
-    float m_ref = -INFINITY, l = 0.f;
-    float rmax_raw = -INFINITY;  // the row's largest visible raw score
     bool ok = true;
-    const int nx = x == 0 ? n_kv0 : n_kv;  // key blocks of this tile
-    for (int j = 0; j < nx; ++j) {
-      int w = 0;
-      if (lane == 0) w = mbar_wait(&s_full[x], j & 1, abort_p) ? 1 : 0;
-      if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
-      tc_fence_after();
-      const int k0 = j * BKV;
-      // keys < kmax are visible to this row
-      int kmax = p.Sk - k0;
-      if (p.causal) kmax = min(kmax, qrow - k0 + 1);
-      // The row's 128 scores come out of TMEM once (four loads, one wait) and stay in
-      // registers for both the max and the exponentials.
-      uint32_t r[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r + c * 32);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_regs_ready(r + c * 32);
-      // no per-element masks when every row of the warp sees the whole block
-      const bool full = __all_sync(0xffffffffu, kmax >= BKV);
-      if (!full) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i >= kmax) r[i] = __float_as_uint(-INFINITY);
+    int cnt = 0;  // key blocks this tile has processed so far (S / P phases)
+    for (int k = 0; ok; ++k) {
+      const int it = item_index(p, k);
+      if (it < 0) break;
+      int qrow, nx;  // this thread's query row, the tile's key blocks
+      {
+        const Item t = item_of(p, it);
+        qrow = t.q0 + x * BQ + row_in_tile;
+        nx = x == 0 ? t.n_kv0 : t.n_kv;
       }
-      float bmax = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) bmax = fmaxf(bmax, __uint_as_float(r[i]));
-      rmax_raw = fmaxf(rmax_raw, bmax);
-      bmax *= p.scale_log2;
-      // lazy rescale: move the reference max only when it grows by more than 8.  The
-      // decision is per row (lane); the TMEM rescale of O is warp-collective, so the whole
-      // warp runs it whenever any lane needs it, with alpha = 1 for the others.
-      float alpha = 1.f;
-      if (bmax > m_ref + 8.f) {
-        if (j > 0 && m_ref != -INFINITY) alpha = ex2_approx(m_ref - bmax);
-        m_ref = bmax;
-      }
-      l *= alpha;
-      if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(t_o + c * 32, o);
-          tmem_wait_ld();
-          tmem_regs_ready(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(t_o + c * 32, o);
+      float m_ref = -INFINITY, l = 0.f;
+      float rmax_raw = -INFINITY;  // the row's largest visible raw score
+      for (int j = 0; j < nx; ++j, ++cnt) {
+        int w = 0;
+        if (lane == 0) w = mbar_wait(&s_full[x], cnt & 1, abort_p) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+        tc_fence_after();
+        const int k0 = j * BKV;
+        // keys < kmax are visible to this row
+        int kmax = p.Sk - k0;
+        if (p.causal) kmax = min(kmax, qrow - k0 + 1);
+        // The row's 128 scores come out of TMEM once (four loads, one wait) and stay in
+        // registers for both the max and the exponentials.
+        uint32_t r[128];
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, r + c * 32);
+        tmem_wait_ld();
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_regs_ready(r + c * 32);
+        // no per-element masks when every row of the warp sees the whole block
+        const bool full = __all_sync(0xffffffffu, kmax >= BKV);
+        if (!full) {
+  #pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i >= kmax) r[i] = __float_as_uint(-INFINITY);
         }
-        tmem_wait_st();
-      }
-      // P = exp2(s * scale_log2 - m_ref) (masked scores are -inf -> 0), packed in pairs
-      // over S columns [0, 64)
-      const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // fully masked row: all P = 0
-      float bsum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float a = ex2_approx(fmaf(__uint_as_float(r[c * 32 + 2 * i]), p.scale_log2, -mr));
-          const float b = ex2_approx(fmaf(__uint_as_float(r[c * 32 + 2 * i + 1]), p.scale_log2, -mr));
-          bsum += a + b;
-          if constexpr (DT == AK_BF16) {
-            __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-            pk[i] = *reinterpret_cast<uint32_t*>(&h);
-          } else {
-            __half2 h = __floats2half2_rn(a, b);
-            pk[i] = *reinterpret_cast<uint32_t*>(&h);
+        float bmax = -INFINITY;
+  #pragma unroll
+        for (int i = 0; i < 128; ++i) bmax = fmaxf(bmax, __uint_as_float(r[i]));
+        rmax_raw = fmaxf(rmax_raw, bmax);
+        bmax *= p.scale_log2;
+        // lazy rescale: move the reference max only when it grows by more than 8.  The
+        // decision is per row (lane); the TMEM rescale of O is warp-collective, so the whole
+        // warp runs it whenever any lane needs it, with alpha = 1 for the others.
+        float alpha = 1.f;
+        if (bmax > m_ref + 8.f) {
+          if (j > 0 && m_ref != -INFINITY) alpha = ex2_approx(m_ref - bmax);
+          m_ref = bmax;
+        }
+        l *= alpha;
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+  #pragma unroll 1
+          for (int c = 0; c < D / 8; ++c) {
+            uint32_t o[8];
+            tmem_ld8(t_o + c * 8, o);
+            tmem_wait_ld();
+            tmem_regs_ready8(o);
+  #pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st8(t_o + c * 8, o);
           }
+          tmem_wait_st();
         }
-        tmem_st16(t_s + c * 16, pk);
+        // P = exp2(s * scale_log2 - m_ref) (masked scores are -inf -> 0), packed in pairs
+        // over S columns [0, 64)
+        const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // fully masked row: all P = 0
+        float bsum = 0.f;
+  #pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t pk[8];
+  #pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float a = ex2_approx(fmaf(__uint_as_float(r[c * 16 + 2 * i]), p.scale_log2, -mr));
+            const float b = ex2_approx(fmaf(__uint_as_float(r[c * 16 + 2 * i + 1]), p.scale_log2, -mr));
+            bsum += a + b;
+            if constexpr (DT == AK_BF16) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+              pk[i] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+              __half2 h = __floats2half2_rn(a, b);
+              pk[i] = *reinterpret_cast<uint32_t*>(&h);
+            }
+          }
+          tmem_st8(t_s + c * 8, pk);
+        }
+        l += bsum;
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[x]);
       }
-      l += bsum;
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[x]);
-    }
-    // epilogue: O / l -> global
-    int w = 0;
-    if (ok && lane == 0) w = mbar_wait(&o_done[x], 0, abort_p) ? 1 : 0;
-    w = __shfl_sync(0xffffffffu, w, 0);
-    if (w) {
+      // epilogue: O / l -> global
+      int w = 0;
+      if (ok && lane == 0) w = mbar_wait(&o_done[x], k & 1, abort_p) ? 1 : 0;
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (!w) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       // reference.py forms the scores in the input dtype: in fp16 a visible score beyond
       // +-65504 (or one that leaves no finite key) turns the row's softmax into NaN there
       const bool nan_row = rmax_raw >= p.ovf || rmax_raw <= -p.ovf;
       const float inv = nan_row ? __int_as_float(0x7fffffff) : (l > 0.f ? 1.f / l : 0.f);
-      T* orow = reinterpret_cast<T*>(p.O) + b * p.o_sb + h * p.o_sh + (int64_t)qrow * p.o_ss;
+      const int bh = it / p.n_qblk;
+      T* orow = reinterpret_cast<T*>(p.O) + (bh / p.H) * p.o_sb + (bh % p.H) * p.o_sh +
+                (int64_t)qrow * p.o_ss;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(t_o + c * 32, r);
         tmem_wait_ld();
         tmem_regs_ready(r);
+        if (c == D / 32 - 1) {  // O has been read: the next item's first P V may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_free[x]);
+        }
         if (qrow < p.Sq) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -367,10 +434,11 @@ static int launch(const AttnShape& a, cudaStream_t st) {
   p.idesc_qk = idesc_f16(fmt, BQ, BKV, false, false);
   p.idesc_pv = idesc_f16(fmt, BQ, D, false, true);
   p.n_qblk = (a.Sq + 2 * BQ - 1) / (2 * BQ);
+  p.n_items = (int)(p.n_qblk * a.B * a.H);
   const cudaError_t attr = smem_optin<attn_kernel<DT, D>>(Cfg<D>::SMEM);
   AK_REQUIRE(attr == cudaSuccess, AK_ERR_LAUNCH, "attention smem attribute: %s",
              cudaGetErrorString(attr));
-  dim3 grid((unsigned)p.n_qblk, (unsigned)(a.B * a.H));
+  const int grid = min(p.n_items, device_info().sm_count);
   attn_kernel<DT, D><<<grid, THREADS, Cfg<D>::SMEM, st>>>(tq, tk, tv, p);
   return launch_status("tc_attention");
 }

@@ -187,6 +187,17 @@ AK_D void tmem_ld32(uint32_t taddr, uint32_t* r) {
         "=r"(r[31])
       : "r"(taddr));
 }
+// Warp-collective load of 32 lanes x 8 consecutive 32-bit TMEM columns.
+AK_D void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+AK_D void tmem_regs_ready8(uint32_t* r) {
+  asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                    "+r"(r[6]), "+r"(r[7]));
+}
 // Warp-collective store of 32 lanes x 32 consecutive 32-bit TMEM columns.
 AK_D void tmem_st32(uint32_t taddr, const uint32_t* r) {
   asm volatile(
@@ -209,6 +220,13 @@ AK_D void tmem_st16(uint32_t taddr, const uint32_t* r) {
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15])
       : "memory");
+}
+// Warp-collective store of 32 lanes x 8 consecutive 32-bit TMEM columns.
+AK_D void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+               "r"(r[7])
+               : "memory");
 }
 AK_D float ex2_approx(float x) {
   float y;
