@@ -293,9 +293,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int i = 0; i < 128; ++i)
             if (i >= kmax) r[i] = __float_as_uint(-INFINITY);
         }
-        float bmax = -INFINITY;
+        // four independent chains of 3-input max (one dependent 128-long chain costs its
+        // latency 128 times)
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   #pragma unroll
-        for (int i = 0; i < 128; ++i) bmax = fmaxf(bmax, __uint_as_float(r[i]));
+        for (int i = 0; i < 128; i += 8)
+  #pragma unroll
+          for (int q = 0; q < 4; ++q)
+            mx[q] = fmax3(mx[q], __uint_as_float(r[i + 2 * q]), __uint_as_float(r[i + 2 * q + 1]));
+        float bmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
         rmax_raw = fmaxf(rmax_raw, bmax);
         bmax *= p.scale_log2;
         // lazy rescale: move the reference max only when it grows by more than 8.  The
@@ -323,15 +329,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         // P = exp2(s * scale_log2 - m_ref) (masked scores are -inf -> 0), packed in pairs
         // over S columns [0, 64)
         const float mr = m_ref == -INFINITY ? 0.f : m_ref;  // fully masked row: all P = 0
-        float bsum = 0.f;
+        float2 sum2[2] = {{0.f, 0.f}, {0.f, 0.f}};  // packed partial sums of P
   #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint32_t pk[8];
   #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float a = ex2_approx(fmaf(__uint_as_float(r[c * 16 + 2 * i]), p.scale_log2, -mr));
-            const float b = ex2_approx(fmaf(__uint_as_float(r[c * 16 + 2 * i + 1]), p.scale_log2, -mr));
-            bsum += a + b;
+            const float2 e = ffma2_bcast(__uint_as_float(r[c * 16 + 2 * i]),
+                                         __uint_as_float(r[c * 16 + 2 * i + 1]), p.scale_log2, -mr);
+            const float a = ex2_approx(e.x), b = ex2_approx(e.y);
+            fadd2_acc(sum2[i & 1], a, b);
             if constexpr (DT == AK_BF16) {
               __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
               pk[i] = *reinterpret_cast<uint32_t*>(&h);
@@ -342,7 +349,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tmem_st8(t_s + c * 8, pk);
         }
-        l += bsum;
+        l += (sum2[0].x + sum2[1].x) + (sum2[0].y + sum2[1].y);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();

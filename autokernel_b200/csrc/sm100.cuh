@@ -233,6 +233,22 @@ AK_D float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// (a, b) * (m, m) + (c, c) as one packed f32x2 FMA (sm_100)
+AK_D float2 ffma2_bcast(float a, float b, float m, float c) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %4};\n"
+      " mov.b64 rc, {%5, %5};\n fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a), "f"(b), "f"(m), "f"(c));
+  return d;
+}
+// acc += (a, b) as one packed f32x2 add (sm_100)
+AK_D void fadd2_acc(float2& acc, float a, float b) {
+  asm("{\n .reg .b64 ra, rb;\n mov.b64 ra, {%0, %1};\n mov.b64 rb, {%2, %3};\n"
+      " add.rn.f32x2 ra, ra, rb;\n mov.b64 {%0, %1}, ra;\n}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "f"(a), "f"(b));
+}
 // max of three floats in one instruction (sm_100)
 AK_D float fmax3(float a, float b, float c) {
   float d;
